@@ -1,0 +1,412 @@
+"""Benchmark of the torchcl B200 GEMM path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg5] [--impl ours|reference]
+
+Default workload: bf16 C = relu(A @ W + bias), M = N = K = 32768,
+W column-sharded over the N ranks (rank r holds W[:, r*N/P:(r+1)*N/P] and its bias
+slice, resident), A replicated, each rank computes its column block with the
+fused epilogue and the blocks are all-gathered over NCCL into a row-major C on
+every rank.  Total work is fixed as N grows ("scaling": "strong").
+Other configs (--config cfg1..cfg4) run on one GPU for the parity/roofline notes.
+
+`value` is device time (CUDA events on the launching stream, max over ranks) with
+inputs resident; `e2e` is the same metric through the C-ABI with pinned host
+buffers: host->device copy of A, the GEMM (+ gather), device->host copy of C.
+`--impl reference` times the CPU port of the reference algorithm (oracle/, k
+ascending fp32 accumulation, all host threads) on a bounded sample of the same
+workload.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import datetime
+import json
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+REPO = pathlib.Path(__file__).resolve().parent
+PKG = REPO / "ojasx-open-source-cuda-_b200"
+for p in (str(REPO), str(PKG)):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+CONFIGS = {
+    # name: (M, N, K, dtype, epilogue unary, bias scale, W scale, A distribution, seed)
+    "cfg1": dict(M=512, N=512, K=512, dtype="f32", act="relu", a="normal", w_scale=1.0, b_scale=1.0, seed=0,
+                 desc="fp32 relu(A@B+bias) 512^3"),
+    "cfg2": dict(M=8192, N=8192, K=8192, dtype="f32", act="gelu", a="uniform", w_scale=1.0, b_scale=0.1,
+                 seed=1, desc="fp32 gelu_tanh(A@B+bias) 8192^3, 3xTF32"),
+    "cfg3": dict(M=8192, N=11008, K=4096, dtype="bf16", act="silu", a="normal", w_scale=0.02, b_scale=0.0,
+                 seed=2, desc="bf16 FFN silu(X@W+0) 8192x4096x11008"),
+    "cfg4": dict(M=16, N=14336, K=4096, dtype="bf16", act="silu", a="normal", w_scale=0.02, b_scale=0.0,
+                 seed=3, desc="bf16 skinny decode silu(X@W+bias) M=16 K=4096 N=14336"),
+    "cfg5": dict(M=32768, N=32768, K=32768, dtype="bf16", act="relu", a="normal", w_scale=0.01,
+                 b_scale=0.1, seed=4, desc="bf16 relu(A@W+bias) 32768^3, W column-sharded, C all-gathered"),
+}
+L2_BYTES = 126 * 1024 * 1024
+
+
+def _peaks() -> tuple[dict, str]:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        return json.loads(p.read_text()), "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi samples during the timed region (SM clock, throttle reasons)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.samples: list[list[str]] = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.FIELDS}",
+                                      "--format=csv,noheader,nounits"], capture_output=True, text=True,
+                                     timeout=5).stdout.strip()
+                if out:
+                    self.samples.append([x.strip() for x in out.split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._t:
+            self._t.join(timeout=10)
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4)
+                          if len(s) > 5 + i and s[5 + i].lower().startswith("active")})
+        pw = [float(s[3]) for s in self.samples if s[3].replace(".", "").isdigit()]
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.samples),
+                "power_w_max": max(pw) if pw else None}
+
+
+def _dist_setup():
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and not dist.is_initialized():
+        import torch
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+# ── CPU baseline (reference arm and the cpu_baseline field) ───────────────────
+
+def cpu_baseline(cfg: dict, steps: int = 1) -> dict:
+    """Time the oracle port on a bounded sample of the workload, all host threads."""
+    import numpy as np
+    from oracle import build_oracle
+    build_oracle.build_oracle()
+    from oracle import oracle as O
+    rng = np.random.default_rng(cfg["seed"])
+    K = cfg["K"]
+    # sample: an [ms, ns] block of C with the full K (ascending-k fp32 accumulation)
+    ms = min(cfg["M"], 256 if K >= 16384 else 512)
+    ns = min(cfg["N"], 256 if K >= 16384 else 1024)
+    A = rng.standard_normal((ms, K), dtype=np.float32)
+    B = (rng.standard_normal((K, ns), dtype=np.float32) * cfg["w_scale"]).astype(np.float32)
+    bias = rng.standard_normal(ns, dtype=np.float32) * cfg["b_scale"]
+    half = cfg["dtype"] == "bf16"
+    if half:
+        A, B, bias = O.bf16_bits(A), O.bf16_bits(B), O.bf16_bits(bias)
+    dt = O.BF16 if half else O.F32
+    threads = os.cpu_count() or 1
+    times = []
+    for _ in range(max(1, steps)):
+        t0 = time.perf_counter()
+        O.gemm(A, B, dtype_a=dt, dtype_b=dt, dtype_c=dt, operand=bias, operand_kind="row",
+               operand_dtype=dt, unary=[cfg["act"]], threads=threads)
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    flops = 2.0 * ms * ns * K
+    return {"value": flops / t / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"C[0:{ms}, 0:{ns}] with full K={K} ({'bf16 widened to fp32' if half else 'fp32'}, "
+                      f"k ascending, fp32 accumulate, {cfg['act']} epilogue), median of {len(times)}",
+            "seconds_per_sample": t}
+
+
+def run_reference(args, cfg, world, rank):
+    if rank != 0:
+        return 0
+    t0 = time.perf_counter()
+    for _ in range(args.warmup):
+        cpu_baseline(cfg, 1)
+    cb = cpu_baseline(cfg, args.steps)
+    line = {"impl": "reference", "metric": _metric(cfg), "value": cb["value"], "unit": "TFLOP/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": cb["seconds_per_sample"] * 1e3, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": cfg["dtype"], "data": "synthetic",
+            "config": _config_block(args, cfg, world),
+            "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": cb["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+            "wall_s": time.perf_counter() - t0}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def _metric(cfg) -> str:
+    return f"fused GEMM+epilogue TFLOP/s ({cfg['desc']})"
+
+
+def _config_block(args, cfg, world) -> dict:
+    return {"workload": f"{args.config}: {cfg['desc']}", "M": cfg["M"], "N": cfg["N"], "K": cfg["K"],
+            "epilogue": f"{cfg['act']}(acc + bias[N])",
+            "parallelism": f"N-shard{world}" if world > 1 else "single GPU",
+            "l2": "inputs larger than L2" if cfg["K"] * cfg["N"] * (2 if cfg["dtype"] == "bf16" else 4) > L2_BYTES
+                  else "L2 flushed (256 MiB write) between timed iterations"}
+
+
+# ── our implementation ──────────────────────────────────────────────────────
+
+def run_ours(args, cfg, world, rank, local):
+    import torch
+    import torch.distributed as dist
+    from torchcl import _lib as L
+
+    lib = L.lib()
+    torch.cuda.set_device(local)
+    info = L.DeviceInfo()
+    L.check(lib.ojx_init(local, ctypes.byref(info)), "ojx_init")
+    dev = torch.device("cuda", local)
+    tdt = torch.bfloat16 if cfg["dtype"] == "bf16" else torch.float32
+    code = L.BF16 if tdt == torch.bfloat16 else L.F32
+    es = 2 if tdt == torch.bfloat16 else 4
+    M, N, K = cfg["M"], cfg["N"], cfg["K"]
+    if N % world:
+        raise SystemExit(f"N={N} is not divisible by {world} ranks")
+    Nl = N // world
+    g = torch.Generator(device=dev).manual_seed(cfg["seed"])
+    if cfg["a"] == "uniform":
+        A = (torch.rand(M, K, device=dev, generator=g) * 2 - 1).to(tdt)
+    else:
+        A = torch.randn(M, K, device=dev, generator=g).to(tdt)
+    # W generated column block by column block so every rank draws the same full W
+    W = None
+    for r in range(world):
+        blk = (torch.randn(K, Nl, device=dev, generator=g) * cfg["w_scale"]).to(tdt)
+        if r == rank:
+            W = blk
+        else:
+            del blk
+    bias_full = (torch.randn(N, device=dev, generator=g) * cfg["b_scale"]).to(tdt)
+    bias = bias_full[rank * Nl:(rank + 1) * Nl].contiguous()
+    C_local = torch.empty(M, Nl, device=dev, dtype=tdt)
+    C = torch.empty(M, N, device=dev, dtype=tdt) if world > 1 else C_local
+    gathered = torch.empty(world * M * Nl, device=dev, dtype=tdt) if world > 1 else None
+    flush = torch.empty(256 * 1024 * 1024, device=dev, dtype=torch.uint8)
+    needs_flush = K * Nl * es < L2_BYTES
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+
+    d = L.GemmDesc()
+    d.M, d.N, d.K = M, Nl, K
+    d.dtype_a = d.dtype_b = d.dtype_c = d.dtype_operand = code
+    d.a, d.b, d.c, d.operand = A.data_ptr(), W.data_ptr(), C_local.data_ptr(), bias.data_ptr()
+    d.operand_kind, d.binary_op = L.OPERAND_ROW, L.BINARY["add"]
+    d.n_unary, d.unary[0] = 1, L.UNARY[cfg["act"]]
+    d.fp32_mode = L.FP32_3XTF32 if code == L.F32 and M > 16 else L.FP32_AUTO
+
+    def gemm():
+        L.check(lib.ojx_gemm(ctypes.byref(d), sp), "ojx_gemm")
+
+    def gather():
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, C_local.view(-1))
+            C.view(M, world, Nl).copy_(gathered.view(world, M, Nl).transpose(0, 1))
+
+    # warm-up
+    for _ in range(args.warmup):
+        gemm()
+        gather()
+    torch.cuda.synchronize(dev)
+    route = L.ROUTES.get(lib.ojx_last_route())
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
+           torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    launches0 = lib.ojx_kernel_launch_count()
+    with ClockSampler(local) as clk:
+        for i in range(args.steps):
+            if needs_flush:
+                flush.zero_()
+            ev[i][0].record(stream)
+            gemm()
+            ev[i][1].record(stream)
+            gather()
+            ev[i][2].record(stream)
+        torch.cuda.synchronize(dev)
+    launches = lib.ojx_kernel_launch_count() - launches0
+    L.check(lib.ojx_poll_device_error(), "device error")
+    step_ms = sum(e[0].elapsed_time(e[2]) for e in ev)
+    gemm_ms = [e[0].elapsed_time(e[1]) for e in ev]
+    t = torch.tensor([step_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.barrier()
+    total_ms = float(t.item())
+    flops_total = 2.0 * M * N * K
+    value = flops_total * args.steps / (total_ms / 1e3) / 1e12
+
+    # e2e through the C-ABI with pinned host buffers
+    e2e = e2e_measure(args, lib, L, A, C, M, K, N, es, gemm, gather, world, dev, stream)
+
+    peaks, peak_kind = _peaks()
+    avg_gemm_ms = statistics.mean(gemm_ms)
+    per_launch_flops = 2.0 * M * Nl * K
+    achieved = per_launch_flops / (avg_gemm_ms / 1e3) / 1e12
+    sustained = avg_gemm_ms * args.steps > 1000.0
+    peak = peaks.get("bf16_tflops_sustained" if sustained else "bf16_tflops", 1590.0)
+    if code == L.F32:
+        # 3xTF32 runs three tf32 MMAs (half the bf16 rate each) per fp32 multiply-add
+        peak = peak / 2 / 3
+    roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+            "frac": achieved / peak, "traffic": _traffic(args.config, route),
+            "kernel": f"ojx route {route}", "peak_source": f"{peak_kind} "
+            f"{'bf16_tflops_sustained' if sustained else 'bf16_tflops'}"
+            f"{' / 6 (3xTF32 effective)' if code == L.F32 else ''}",
+            "algorithmic_flop_per_launch": per_launch_flops, "avg_launch_ms": avg_gemm_ms}
+    if cfg["dtype"] == "bf16" and M <= 16:
+        bytes_per = es * (M * K + K * Nl + Nl + M * Nl)
+        gbs = bytes_per / (avg_gemm_ms / 1e3) / 1e9
+        roof.update({"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": gbs / peaks["hbm_gbs"], "algorithmic_bytes_per_launch": bytes_per,
+                     "peak_source": f"{peak_kind} hbm_gbs"})
+
+    if rank == 0:
+        cb = cpu_baseline(cfg, 1) if world == 1 else None
+        clocks = clk.summary()
+        line = {"metric": _metric(cfg), "value": value, "unit": "TFLOP/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                "dtype": cfg["dtype"], "data": "synthetic (seeded torch.Generator on device)",
+                "config": _config_block(args, cfg, world), "route": route, "roofline": roof,
+                "cpu_baseline": ({k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+                                 if cb else None),
+                "e2e": e2e, "gpu_launches": int(launches),
+                "clocks": {k: clocks[k] for k in ("sm_mhz", "sm_max_mhz", "reasons")},
+                "clock_samples": clocks.get("samples"), "power_w_max": clocks.get("power_w_max")}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def e2e_measure(args, lib, L, A, C, M, K, N, es, gemm, gather, world, dev, stream):
+    """Same metric end to end: pinned host A -> device, GEMM (+gather), C -> pinned host."""
+    import torch
+    import torch.distributed as dist
+    a_bytes = M * K * es
+    c_bytes = M * N * es
+    ha, hc = ctypes.c_void_p(), ctypes.c_void_p()
+    L.check(lib.ojx_host_alloc(a_bytes, ctypes.byref(ha)), "pinned A")
+    L.check(lib.ojx_host_alloc(c_bytes, ctypes.byref(hc)), "pinned C")
+    sp = stream.cuda_stream
+    # host copy of this step's input
+    L.check(lib.ojx_memcpy_d2h(ha.value, A.data_ptr(), a_bytes, sp))
+    torch.cuda.synchronize(dev)
+
+    def step():
+        L.check(lib.ojx_memcpy_h2d(A.data_ptr(), ha.value, a_bytes, sp), "h2d")
+        gemm()
+        gather()
+        L.check(lib.ojx_memcpy_d2h(hc.value, C.data_ptr(), c_bytes, sp), "d2h")
+
+    steps = max(2, min(args.steps, 5))
+    step()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    torch.cuda.synchronize(dev)
+    dt = time.perf_counter() - t0
+    t = torch.tensor([dt], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dt = float(t.item())
+    lib.ojx_host_free(ha.value)
+    lib.ojx_host_free(hc.value)
+    flops = 2.0 * M * N * K * steps
+    return {"value": flops / dt / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": a_bytes,
+            "d2h_bytes_per_step": c_bytes, "steps": steps,
+            "note": "C-ABI with pinned host buffers; host clock around synchronised steps"}
+
+
+def _traffic(config: str, route: str):
+    """DRAM bytes per launch from the committed ncu summary, when one exists."""
+    p = REPO / "profiles" / "traffic.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text()).get(config)
+        except Exception:
+            return None
+    return None
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", default="cfg5", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--m", type=int, default=None, help="override M (e.g. cfg4 M in {1,4,16})")
+    ap.add_argument("--size", type=int, default=None, help="override M=N=K (cfg2 sweep)")
+    args = ap.parse_args()
+    cfg = dict(CONFIGS[args.config])
+    if args.m is not None:
+        cfg["M"] = args.m
+    if args.size is not None:
+        cfg["M"] = cfg["N"] = cfg["K"] = args.size
+    if args.m is not None or args.size is not None:
+        cfg["desc"] += f" [M={cfg['M']} N={cfg['N']} K={cfg['K']}]"
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        return run_reference(args, cfg, world, rank)
+    world, rank, local = _dist_setup()
+    if world > 1 and args.config != "cfg5" and args.config != "cfg4":
+        if rank == 0:
+            print(json.dumps({"error": f"{args.config} runs on one GPU"}))
+        return 0
+    return run_ours(args, cfg, world, rank, local)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

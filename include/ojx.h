@@ -1,0 +1,224 @@
+/*
+ * ojx.h — C-ABI of libojx.so, the B200 (sm_100a) runtime and GEMM engine that
+ * backs the `torchcl` Python package (torchcl.matmul / torchcl.blas.gemm and the
+ * lazily fused elementwise epilogue).
+ *
+ * Every function returns an int status (OJX_OK == 0).  On failure a
+ * thread-local message is available from ojx_last_error().  All pointers are
+ * plain device (or host) addresses; no PyTorch types cross this boundary.
+ *
+ * Each declaration names the reference interface it replaces (path:line inside
+ * the OjasX project).  The reference implements these in Python over pyopencl;
+ * here they are native C++/CUDA.
+ */
+#ifndef OJX_H_
+#define OJX_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define OJX_ABI_VERSION 1
+
+/* ── status codes ─────────────────────────────────────────────────────────
+ * OJX_ERR_INVALID  -> ValueError   (torchcl/api.py:433-439 raises on bad shapes)
+ * OJX_ERR_OOM      -> MemoryError  (after evict-and-retry, torchcl/runtime/memory.py:109-115)
+ * OJX_ERR_TIMEOUT  -> RuntimeError (a bounded device-side wait expired; the kernel returned)
+ * OJX_ERR_CUDA     -> RuntimeError (any CUDA runtime/driver failure)
+ */
+enum {
+  OJX_OK = 0,
+  OJX_ERR_INVALID = 1,
+  OJX_ERR_OOM = 2,
+  OJX_ERR_CUDA = 3,
+  OJX_ERR_TIMEOUT = 4,
+  OJX_ERR_UNSUPPORTED = 5,
+  OJX_ERR_NOT_INITIALIZED = 6
+};
+
+/* element types */
+enum { OJX_F32 = 0, OJX_BF16 = 1, OJX_F16 = 2 };
+
+/* unary epilogue ops; the set and formulas of torchcl/jit/compiler.py:33-45 */
+enum {
+  OJX_UN_NONE = 0,
+  OJX_UN_RELU = 1,
+  OJX_UN_SIGMOID = 2,
+  OJX_UN_TANH = 3,
+  OJX_UN_NEG = 4,
+  OJX_UN_ABS = 5,
+  OJX_UN_EXP = 6,
+  OJX_UN_LOG = 7,
+  OJX_UN_SQRT = 8,
+  OJX_UN_SILU = 9,
+  OJX_UN_GELU = 10, /* tanh approximation, torchcl/jit/compiler.py:43 */
+  OJX_UN_SQUARE = 11
+};
+
+/* binary epilogue ops; torchcl/jit/compiler.py:47-52 */
+enum { OJX_BIN_NONE = 0, OJX_BIN_ADD = 1, OJX_BIN_SUB = 2, OJX_BIN_MUL = 3, OJX_BIN_DIV = 4 };
+
+/* shape of the epilogue's second operand */
+enum {
+  OJX_OPERAND_NONE = 0,
+  OJX_OPERAND_ROW = 1,  /* bias[N], broadcast over rows (matmul.cl:218 `bias[out_col + j]`) */
+  OJX_OPERAND_FULL = 2  /* X[M,N] with leading dimension ld_operand (fused binary of api.py:109-128) */
+};
+
+/* how an fp32 GEMM is computed */
+enum {
+  OJX_FP32_AUTO = 0,   /* 3xTF32 on tcgen05 when the shape allows, FFMA otherwise */
+  OJX_FP32_3XTF32 = 1, /* split x = hi + lo (both tf32), C = Ah*Bh + Ah*Bl + Al*Bh, fp32 accumulate */
+  OJX_FP32_FFMA = 2    /* SIMT fp32 FMA, k ascending per output element */
+};
+
+#define OJX_MAX_UNARY 8
+
+/* One GEMM with its fused epilogue:
+ *   acc[m,n] = sum_k op(A)[m,k] * op(B)[k,n]              (fp32 accumulate)
+ *   v        = operand_kind ? bin(acc, X) : acc           (bin(X, acc) if operand_is_lhs)
+ *   v        = unary[n_unary-1](...unary[0](v))
+ *   C[m,n]   = convert(v, dtype_c)
+ * op(A) = A (row-major [M,K], lda) or A^T (A stored row-major [K,M]) when trans_a.
+ * op(B) = B (row-major [K,N], ldb) or B^T (B stored row-major [N,K]) when trans_b.
+ * Replaces OpenCLEngine.run_matmul / run_matmul_bias / run_linear / run_matmul_fp16
+ * (torchcl/ops/engine.py:156-255, 351-392) plus the JIT's second launch
+ * (torchcl/jit/compiler.py:99-133): one launch, one store.
+ */
+typedef struct ojx_gemm_desc {
+  int64_t M, N, K;
+  int32_t dtype_a, dtype_b, dtype_c, dtype_operand; /* OJX_F32 / OJX_BF16 / OJX_F16 */
+  int32_t trans_a, trans_b;
+  int64_t lda, ldb, ldc, ld_operand; /* leading dimensions in elements; 0 = dense */
+  const void* a;
+  const void* b;
+  void* c;
+  const void* operand; /* bias[N] or X[M,N]; may be NULL when operand_kind == NONE */
+  int32_t operand_kind; /* OJX_OPERAND_* */
+  int32_t binary_op;    /* OJX_BIN_*; ADD when a bias is given */
+  int32_t operand_is_lhs; /* 1: v = bin(X, acc) (e.g. sub(X, matmul(A,B))) */
+  int32_t n_unary;
+  int32_t unary[OJX_MAX_UNARY];
+  int32_t fp32_mode; /* OJX_FP32_* */
+  int32_t flags;     /* OJX_GEMM_FLAG_* */
+} ojx_gemm_desc;
+
+/* route selection overrides (tests and benchmarks) */
+#define OJX_GEMM_FLAG_FORCE_SIMT 0x1   /* SIMT kernel for any dtype */
+#define OJX_GEMM_FLAG_NO_SKINNY 0x2    /* never take the split-K skinny route */
+#define OJX_GEMM_FLAG_FORCE_SKINNY 0x4 /* skinny route when M <= 16 even if a tile kernel would fit */
+
+/* Which kernel family ojx_gemm used for its most recent call on this thread. */
+enum {
+  OJX_ROUTE_NONE = 0,
+  OJX_ROUTE_TC_F16 = 1,   /* tcgen05 kind::f16 tile GEMM (bf16/fp16) */
+  OJX_ROUTE_TC_3XTF32 = 2,/* tcgen05 kind::tf32, three MMAs per k-step */
+  OJX_ROUTE_SKINNY = 3,   /* tcgen05 swap-AB stream-K skinny GEMM */
+  OJX_ROUTE_SIMT = 4      /* SIMT FMA GEMM (any shape, any stride) */
+};
+
+typedef struct ojx_device_info {
+  char name[256];
+  int32_t device;
+  int32_t cc_major, cc_minor;
+  int32_t sm_count;
+  int64_t total_mem_bytes;
+  int64_t l2_bytes;
+  int32_t max_smem_per_block;
+  int32_t clock_khz;
+} ojx_device_info;
+
+typedef struct ojx_pool_stats {
+  int64_t alloc_count;            /* fresh cudaMalloc calls */
+  int64_t reuse_count;            /* requests served from a cached block */
+  int64_t free_count;
+  int64_t active_bytes;           /* capacity of blocks handed out */
+  int64_t cached_bytes;           /* capacity of blocks parked in bins */
+  int64_t peak_bytes;
+  int64_t total_allocated_bytes;  /* sum of all cudaMalloc sizes */
+  int64_t active_buffers;
+  int64_t evictions;              /* evict-and-retry events after an OOM */
+} ojx_pool_stats;
+
+/* Streams are plain cudaStream_t values; NULL is the legacy default stream. */
+typedef void* ojx_stream;
+typedef void* ojx_event;
+
+/* ── runtime (replaces torchcl/runtime/context.py:26-146) ─────────────── */
+int ojx_abi_version(void);
+int ojx_device_count(int* count);                       /* context.py:131-140 is_available */
+int ojx_init(int device, ojx_device_info* info);        /* context.py:26-100 init_opencl, 169-186 */
+int ojx_current_device(int* device);
+int ojx_synchronize(void);                               /* context.py:143-146 synchronize */
+const char* ojx_last_error(void);                        /* thread-local message of the last failure */
+int ojx_poll_device_error(void);                         /* reads and clears the kernels' error word */
+int ojx_set_wait_budget(uint64_t cycles);                /* bound of every device-side spin wait */
+uint64_t ojx_kernel_launch_count(void);                  /* kernels this library launched so far */
+int ojx_last_route(void);                                /* OJX_ROUTE_* of this thread's last ojx_gemm */
+
+/* ── caching allocator (replaces torchcl/runtime/memory.py:61-203 CLBufferPool) ── */
+int ojx_malloc(size_t nbytes, void** dptr, size_t* capacity); /* memory.py:85-127 allocate */
+int ojx_free(void* dptr);                                      /* memory.py:129-137 free */
+int ojx_empty_cache(void);                                     /* memory.py:139-143 */
+int ojx_pool_stats_get(ojx_pool_stats* out);                   /* memory.py:198-203 get_stats */
+int ojx_pool_bin_size(size_t nbytes, size_t* capacity);        /* memory.py:20-24 _next_power_of_two */
+int ojx_pool_debug_fail_next(int64_t n_allocs);                /* test hook: the next n cudaMalloc calls fail */
+
+/* ── copies (memory.py:145-196) ───────────────────────────────────────── */
+int ojx_memcpy_h2d(void* dst, const void* src, size_t nbytes, ojx_stream s);
+int ojx_memcpy_d2h(void* dst, const void* src, size_t nbytes, ojx_stream s);
+int ojx_memcpy_d2d(void* dst, const void* src, size_t nbytes, ojx_stream s);
+int ojx_memset(void* dst, int value, size_t nbytes, ojx_stream s); /* memory.py:192-196 zero_fill */
+int ojx_host_alloc(size_t nbytes, void** host_ptr);                 /* pinned host memory */
+int ojx_host_free(void* host_ptr);
+
+/* ── streams and events (replaces torchcl/runtime/stream.py:32-132) ───── */
+int ojx_stream_create(ojx_stream* s);
+int ojx_stream_destroy(ojx_stream s);
+int ojx_stream_synchronize(ojx_stream s);
+int ojx_stream_wait_event(ojx_stream s, ojx_event e);
+int ojx_event_create(ojx_event* e, int enable_timing);
+int ojx_event_destroy(ojx_event e);
+int ojx_event_record(ojx_event e, ojx_stream s);
+int ojx_event_query(ojx_event e, int* done);
+int ojx_event_synchronize(ojx_event e);
+int ojx_event_elapsed_ms(ojx_event start, ojx_event end, float* ms);
+
+/* ── compute ──────────────────────────────────────────────────────────── */
+/* GEMM + fused epilogue.  Replaces engine.py:156-255 and 351-392 and
+ * the matmul.cl kernels matmul_reg_tiled_f32 (19-120), matmul_reg_tiled_bias_f32
+ * (123-224), linear_forward_tiled_f32 (297-343), matmul_naive_f32 (346-364),
+ * matmul_bias_f32 (366-385), matmul_tiled_fp16 (422-463).  Asynchronous on s. */
+int ojx_gemm(const ojx_gemm_desc* d, ojx_stream s);
+
+/* Elementwise fusion: out[i] = u_n(...u_1(bin(a[i], b[i]))) over a flat range.
+ * b == NULL -> unary chain only.  Replaces JITCompiler.fuse_elementwise_chain and
+ * fuse_binary_then_unary (torchcl/jit/compiler.py:64-133). */
+int ojx_elementwise(void* out, int32_t dtype_out, const void* a, int32_t dtype_a,
+                    const void* b, int32_t dtype_b, int32_t binary_op,
+                    const int32_t* unary, int32_t n_unary, int64_t n, ojx_stream s);
+
+/* out[cols, rows] = in[rows, cols]^T.  Replaces run_transpose (engine.py:332-349,
+ * matmul.cl:387-398 transpose_f32). */
+int ojx_transpose(void* out, const void* in, int64_t rows, int64_t cols, int32_t dtype, ojx_stream s);
+
+/* out[i] = value.  Replaces run_fill (engine.py run_fill, elementwise.cl fill_f32). */
+int ojx_fill(void* out, double value, int64_t n, int32_t dtype, ojx_stream s);
+
+/* dtype conversion.  Replaces AdaptivePrecision pack/unpack (torchcl/liquid/precision.py:68-103,
+ * precision.cl:7-27). */
+int ojx_cast(void* out, int32_t dtype_out, const void* in, int32_t dtype_in, int64_t n, ojx_stream s);
+
+/* Test hook: the next ojx_gemm on a tcgen05 route runs with its TMA producer
+ * silenced, so the MMA warp's bounded wait must expire and the kernel must
+ * return with OJX_ERR_TIMEOUT recorded (read it with ojx_poll_device_error). */
+int ojx_debug_silence_producer_once(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* OJX_H_ */

@@ -1,0 +1,472 @@
+// gemm_tc.cu — persistent, warp-specialised tcgen05 GEMM with the fused epilogue.
+//
+// Replaces the reference's matmul_reg_tiled_f32 / matmul_reg_tiled_bias_f32 /
+// linear_forward_tiled_f32 / matmul_tiled_fp16 (torchcl/kernels/matmul.cl:19-224,
+// 297-343, 422-463) and the JIT's second elementwise launch
+// (torchcl/jit/compiler.py:99-133): C = epilogue(A·B) in one launch, one store.
+//
+// CTA = 192 threads, one CTA per SM, grid = min(#tiles, #SMs), tiles walked with a
+// stride of gridDim.x in a grouped (8 M-blocks) raster for L2 reuse.
+//   warp 0      TMA producer: STAGES-deep ring of 128B-swizzled A/B tiles
+//   warp 1      TMEM owner + single-thread tcgen05.mma issuer
+//   warps 2..5  epilogue: TMEM -> registers -> bias/binary/unary chain -> store
+// The accumulator is double-buffered in TMEM (2 x BN fp32 columns), so the
+// epilogue of tile i overlaps the MMAs of tile i+1.
+//
+// KIND 0: bf16/fp16 operands, tcgen05 kind::f16, either operand K- or MN-major
+//         (transposes are expressed in the TMA/UMMA descriptors, never copied).
+// KIND 1: fp32 via 3xTF32: A = Ah + Al, B = Bh + Bl (tf32 parts produced by
+//         split_tf32_kernel), acc += Al·Bh + Ah·Bl + Ah·Bh per k-step, kind::tf32.
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <algorithm>
+#include "sm100.cuh"
+#include "epilogue.cuh"
+#include "internal.h"
+#include "tmap.h"
+
+namespace ojx {
+
+constexpr int TC_BM = 128;
+constexpr int TC_THREADS = 192;
+
+template <int KIND, int BN, int STAGES>
+struct TcLayout {
+  static constexpr int ELEM = KIND == 0 ? 2 : 4;
+  static constexpr int BK = 128 / ELEM;  // elements in one 128-byte swizzle row
+  static constexpr int A_BYTES = TC_BM * 128;
+  static constexpr int B_BYTES = BN * 128;
+  static constexpr int NPART = KIND == 0 ? 1 : 2;  // tf32: hi and lo copies
+  static constexpr int STAGE_BYTES = (A_BYTES + B_BYTES) * NPART;
+  static constexpr uint32_t TMEM_COLS = 2 * BN;
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
+  static_assert(STAGE_BYTES % 1024 == 0, "stages must keep 1024-byte alignment");
+  static_assert((2 * STAGES + 6) * 8 + 8 <= BAR_BYTES, "barrier area too small");
+};
+
+// Grouped raster: 8 consecutive M-blocks share each N-block sweep.
+__device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int& mb, int& nb) {
+  constexpr int GROUP = 8;
+  const int span = GROUP * tiles_n;
+  const int g = tile / span;
+  const int first_m = g * GROUP;
+  const int gsize = min(tiles_m - first_m, GROUP);
+  const int r = tile - g * span;
+  mb = first_m + r % gsize;
+  nb = r / gsize;
+}
+
+// Descriptor of one 32-byte k-step of an operand tile.
+//  K-major : rows of 128 B along k, 8-row groups 1024 B apart; a k-step moves 32 B.
+//  MN-major: rows of 128 B (64 elements) along M/N, one row per k; 64-wide MN
+//            blocks are `BK*128` bytes apart (LBO), 8-k groups 1024 B apart (SBO);
+//            a k-step of 16 (f16) rows moves 2048 B.
+template <int MN, int BK>
+__device__ __forceinline__ uint64_t operand_desc(uint32_t base, int ks) {
+  if (MN) return make_sw128_desc(base + ks * 2048, BK * 128, 1024);
+  return make_sw128_desc(base + ks * 32, 16, 1024);
+}
+
+// Loads of one operand tile (rows = 128 for A, BN for B) at (mn0, k0).
+template <int MN, int BK, int ROWS>
+__device__ __forceinline__ void load_operand(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                             int mn0, int k0) {
+  if (MN) {
+#pragma unroll
+    for (int j = 0; j < ROWS / 64; ++j) tma_load_2d(dst + j * (BK * 128), map, bar, mn0 + 64 * j, k0);
+  } else {
+    tma_load_2d(dst, map, bar, k0, mn0);
+  }
+}
+
+// Epilogue for 16 consecutive columns of one output row.
+__device__ __forceinline__ void store_row16(const EpiParams& ep, const uint32_t (&r)[16],
+                                            int64_t row, int col0, int N) {
+  float v[16];
+  const bool full = col0 + 16 <= N;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    v[j] = __uint_as_float(r[j]);
+    if (full || col0 + j < N) v[j] = epilogue_value(ep, v[j], row, col0 + j);
+  }
+  const int esz = ep.dtype_c == OJX_F32 ? 4 : 2;
+  char* dst = static_cast<char*>(ep.c) + (row * ep.ldc + col0) * esz;
+  if (full && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+    if (ep.dtype_c == OJX_F32) {
+      float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) d4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    } else {
+      uint32_t p[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (ep.dtype_c == OJX_BF16) {
+          __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+          p[j] = *reinterpret_cast<uint32_t*>(&h);
+        } else {
+          __half2 h = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+          p[j] = *reinterpret_cast<uint32_t*>(&h);
+        }
+      }
+      uint4* d4 = reinterpret_cast<uint4*>(dst);
+      d4[0] = make_uint4(p[0], p[1], p[2], p[3]);
+      d4[1] = make_uint4(p[4], p[5], p[6], p[7]);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (col0 + j < N) store_elem(ep.c, row * ep.ldc + col0 + j, ep.dtype_c, v[j]);
+  }
+}
+
+template <int KIND, int FMT, int A_MN, int B_MN, int BN, int STAGES>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmA2,
+                   const __grid_constant__ CUtensorMap tmB2, const EpiParams ep, const int M,
+                   const int N, const int K, const uint64_t budget, const int silence_producer) {
+  using L = TcLayout<KIND, BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * L::STAGE_BYTES);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(bars + 2 * STAGES + 5);
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 6);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bar0 = smem_u32(bars);
+  // barrier addresses
+  auto full_bar = [&](int s) { return bar0 + 8u * s; };
+  auto empty_bar = [&](int s) { return bar0 + 8u * (STAGES + s); };
+  auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + a); };
+  auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + 2 + a); };
+  const uint32_t done_bar = bar0 + 8u * (2 * STAGES + 4);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull_bar(a), 1);
+      mbar_init(tempty_bar(a), 4);
+    }
+    mbar_init(done_bar, 1);
+    *s_abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    if (KIND == 1) {
+      tma_prefetch_desc(&tmA2);
+      tma_prefetch_desc(&tmB2);
+    }
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(s_tmem), L::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *s_tmem;
+
+  const int tiles_m = (M + TC_BM - 1) / TC_BM;
+  const int tiles_n = (N + BN - 1) / BN;
+  const int num_tiles = tiles_m * tiles_n;
+  const int KB = (K + L::BK - 1) / L::BK;
+
+  if (warp == 0) {
+    // ── TMA producer ──────────────────────────────────────────────────────
+    if (lane == 0 && !silence_producer) {
+      int stage = 0;
+      uint32_t phase = 0, issued = 0, issued_parity = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        int mb, nb;
+        tile_coords(tile, tiles_m, tiles_n, mb, nb);
+        const int m0 = mb * TC_BM, n0 = nb * BN;
+        for (int kb = 0; kb < KB; ++kb) {
+          if (!mbar_wait(empty_bar(stage), phase ^ 1u, budget, s_abort)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = full_bar(stage);
+          mbar_arrive_expect_tx(fb, L::STAGE_BYTES);
+          const uint32_t sA = sbase + stage * L::STAGE_BYTES;
+          const uint32_t sB = sA + L::A_BYTES;
+          const int k0 = kb * L::BK;
+          load_operand<A_MN, L::BK, TC_BM>(sA, &tmA, fb, m0, k0);
+          load_operand<B_MN, L::BK, BN>(sB, &tmB, fb, n0, k0);
+          if (KIND == 1) {
+            load_operand<A_MN, L::BK, TC_BM>(sB + L::B_BYTES, &tmA2, fb, m0, k0);
+            load_operand<B_MN, L::BK, BN>(sB + L::B_BYTES + L::A_BYTES, &tmB2, fb, n0, k0);
+          }
+          issued |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Let every copy this thread issued land before the CTA may exit.
+      for (int s = 0; s < STAGES; ++s)
+        if ((issued >> s) & 1u) mbar_wait_drain(full_bar(s), (issued_parity >> s) & 1u, budget);
+    }
+  } else if (warp == 1) {
+    // ── MMA issuer (one thread) ───────────────────────────────────────────
+    if (lane == 0) {
+      constexpr uint32_t IDESC = make_idesc(FMT, A_MN, B_MN, TC_BM, BN);
+      int stage = 0, acc = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, budget, s_abort)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < KB; ++kb) {
+          if (!mbar_wait(full_bar(stage), phase, budget, s_abort)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sA = sbase + stage * L::STAGE_BYTES;
+          const uint32_t sB = sA + L::A_BYTES;
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks) {
+            const uint64_t ad = operand_desc<A_MN, L::BK>(sA, ks);
+            const uint64_t bd = operand_desc<B_MN, L::BK>(sB, ks);
+            const uint32_t accum = (kb | ks) != 0 ? 1u : 0u;
+            if (KIND == 0) {
+              mma_f16(d, ad, bd, IDESC, accum);
+            } else {
+              const uint64_t ad_lo = operand_desc<A_MN, L::BK>(sB + L::B_BYTES, ks);
+              const uint64_t bd_lo = operand_desc<B_MN, L::BK>(sB + L::B_BYTES + L::A_BYTES, ks);
+              mma_tf32(d, ad_lo, bd, IDESC, accum);  // Al * Bh
+              mma_tf32(d, ad, bd_lo, IDESC, 1u);     // Ah * Bl
+              mma_tf32(d, ad, bd, IDESC, 1u);        // Ah * Bh
+            }
+          }
+          mma_commit(empty_bar(stage));  // smem slot free once these MMAs have read it
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        mma_commit(tfull_bar(acc));  // accumulator ready for the epilogue
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+      // Every MMA issued above must complete before TMEM is released.
+      mma_commit(done_bar);
+      mbar_wait_drain(done_bar, 0, budget);
+    }
+    __syncwarp();
+  } else {
+    // ── epilogue warps 2..5: warp w reads TMEM lanes 32*(w%4) .. +31 ───────
+    const int q = warp & 3;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      if (!mbar_wait(tfull_bar(acc), acc_phase, budget, s_abort)) break;
+      tc_fence_after();
+      int mb, nb;
+      tile_coords(tile, tiles_m, tiles_n, mb, nb);
+      const int64_t row = static_cast<int64_t>(mb) * TC_BM + q * 32 + lane;
+      const int n0 = nb * BN;
+      const uint32_t tbase =
+          tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN / 16; ++c) {
+        const int col0 = n0 + c * 16;
+        if (col0 >= N) break;  // uniform across the warp
+        uint32_t r[16];
+        tmem_ld16(tbase + c * 16, r);
+        tmem_wait_ld();
+        if (row < M) store_row16(ep, r, row, col0, N);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty_bar(acc));
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, L::TMEM_COLS);
+  }
+}
+
+// fp32 -> (hi, lo) tf32 parts, K-major [R][Kp], zero for k >= K.
+// Element (r, k) of the logical operand is src[r*ld + k] (trans == 0) or
+// src[k*ld + r] (trans == 1).  tf32 rounding: cvt.rna (round to nearest, ties away).
+__device__ __forceinline__ float to_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+__global__ void __launch_bounds__(256) split_tf32_kernel(const float* __restrict__ src, int64_t ld,
+                                                         int trans, int R, int K, int Kp,
+                                                         float* __restrict__ hi,
+                                                         float* __restrict__ lo) {
+  __shared__ float tile[32][33];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
+  const int k0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+  if (!trans) {
+    for (int i = ty; i < 32; i += 8) {
+      const int r = r0 + i, k = k0 + tx;
+      if (r < R && k < Kp) {
+        const float v = (k < K) ? src[static_cast<int64_t>(r) * ld + k] : 0.0f;
+        const float h = to_tf32(v);
+        const int64_t o = static_cast<int64_t>(r) * Kp + k;
+        hi[o] = h;
+        lo[o] = to_tf32(v - h);
+      }
+    }
+  } else {
+    for (int i = ty; i < 32; i += 8) {
+      const int k = k0 + i, r = r0 + tx;
+      tile[i][tx] = (k < K && r < R) ? src[static_cast<int64_t>(k) * ld + r] : 0.0f;
+    }
+    __syncthreads();
+    for (int i = ty; i < 32; i += 8) {
+      const int r = r0 + i, k = k0 + tx;
+      if (r < R && k < Kp) {
+        const float v = tile[tx][i];
+        const float h = to_tf32(v);
+        const int64_t o = static_cast<int64_t>(r) * Kp + k;
+        hi[o] = h;
+        lo[o] = to_tf32(v - h);
+      }
+    }
+  }
+}
+
+// ── host side ────────────────────────────────────────────────────────────────
+
+EpiParams make_epi(const ojx_gemm_desc& d) {
+  EpiParams ep{};
+  ep.c = d.c;
+  ep.ldc = d.ldc;
+  ep.operand = d.operand;
+  ep.ld_operand = d.ld_operand;
+  ep.dtype_c = d.dtype_c;
+  ep.dtype_operand = d.dtype_operand;
+  ep.operand_kind = d.operand_kind;
+  ep.binary_op = d.binary_op;
+  ep.operand_is_lhs = d.operand_is_lhs;
+  ep.n_unary = d.n_unary;
+  for (int i = 0; i < OJX_MAX_UNARY; ++i) ep.unary[i] = i < d.n_unary ? d.unary[i] : 0;
+  return ep;
+}
+
+template <int KIND, int FMT, int A_MN, int B_MN, int BN, int STAGES>
+static int run_tc(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& a2,
+                  const CUtensorMap& b2, const EpiParams& ep, int M, int N, int K,
+                  cudaStream_t s) {
+  using L = TcLayout<KIND, BN, STAGES>;
+  auto kern = tc_gemm_kernel<KIND, FMT, A_MN, B_MN, BN, STAGES>;
+  int st = cuda_status(
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM_BYTES),
+      "cudaFuncSetAttribute(tc_gemm)");
+  if (st) return st;
+  const DeviceProps& p = current_props();
+  const long tiles = static_cast<long>((M + TC_BM - 1) / TC_BM) * ((N + BN - 1) / BN);
+  const int grid = static_cast<int>(std::min<long>(tiles, p.sm_count));
+  const int silence = g_silence_producer_once.exchange(0);
+  kern<<<grid, TC_THREADS, L::SMEM_BYTES, s>>>(a, b, a2, b2, ep, M, N, K, g_wait_budget.load(),
+                                               silence);
+  g_launches.fetch_add(1);
+  return cuda_status(cudaGetLastError(), "tc_gemm launch");
+}
+
+bool tc_gemm_supported(const ojx_gemm_desc& d) {
+  if (d.dtype_a != d.dtype_b || (d.dtype_a != OJX_BF16 && d.dtype_a != OJX_F16)) return false;
+  if (d.K <= 0 || d.M > INT32_MAX || d.N > INT32_MAX || d.K > INT32_MAX) return false;
+  if (reinterpret_cast<uintptr_t>(d.a) % 16 || reinterpret_cast<uintptr_t>(d.b) % 16) return false;
+  if ((d.lda * 2) % 16 || (d.ldb * 2) % 16) return false;
+  return true;
+}
+
+int launch_tc_gemm(const ojx_gemm_desc& d, cudaStream_t s) {
+  const int M = static_cast<int>(d.M), N = static_cast<int>(d.N), K = static_cast<int>(d.K);
+  const CUtensorMapDataType tdt =
+      d.dtype_a == OJX_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const DeviceProps& p = current_props();
+  // BN = 256 unless that leaves most SMs idle.
+  const long tiles256 = static_cast<long>((M + 127) / 128) * ((N + 255) / 256);
+  const int BN = tiles256 >= p.sm_count ? 256 : 128;
+  CUtensorMap ta, tb;
+  int st;
+  // A: K-major [M,K] (box 64k x 128m) or MN-major [K,M] (box 64m x 64k).
+  if (!d.trans_a)
+    st = make_tmap_2d_sw128(&ta, tdt, 2, d.a, K, M, d.lda * 2, 64, 128);
+  else
+    st = make_tmap_2d_sw128(&ta, tdt, 2, d.a, M, K, d.lda * 2, 64, 64);
+  if (st) return st;
+  // B: MN-major [K,N] (box 64n x 64k) or K-major [N,K] (box 64k x BN).
+  if (!d.trans_b)
+    st = make_tmap_2d_sw128(&tb, tdt, 2, d.b, N, K, d.ldb * 2, 64, 64);
+  else
+    st = make_tmap_2d_sw128(&tb, tdt, 2, d.b, K, N, d.ldb * 2, 64, BN);
+  if (st) return st;
+  const EpiParams ep = make_epi(d);
+  const bool bf = d.dtype_a == OJX_BF16;
+  const int am = d.trans_a ? 1 : 0, bm = d.trans_b ? 0 : 1;
+#define OJX_TC_CASE(FMTV, AMN, BMN, BNV)                                                  \
+  if ((bf ? 1 : 0) == FMTV && am == AMN && bm == BMN && BN == BNV)                         \
+    return run_tc<0, FMTV, AMN, BMN, BNV, BNV == 256 ? 4 : 6>(ta, tb, ta, tb, ep, M, N, K, s);
+#define OJX_TC_BN(FMTV, AMN, BMN) \
+  OJX_TC_CASE(FMTV, AMN, BMN, 256) OJX_TC_CASE(FMTV, AMN, BMN, 128)
+  OJX_TC_BN(1, 0, 1) OJX_TC_BN(1, 0, 0) OJX_TC_BN(1, 1, 1) OJX_TC_BN(1, 1, 0)
+  OJX_TC_BN(0, 0, 1) OJX_TC_BN(0, 0, 0) OJX_TC_BN(0, 1, 1) OJX_TC_BN(0, 1, 0)
+#undef OJX_TC_BN
+#undef OJX_TC_CASE
+  return set_error(OJX_ERR_UNSUPPORTED, "no tcgen05 GEMM instance for this layout");
+}
+
+int launch_tc_gemm_3xtf32(const ojx_gemm_desc& d, cudaStream_t s) {
+  const int M = static_cast<int>(d.M), N = static_cast<int>(d.N), K = static_cast<int>(d.K);
+  const int Kp = (K + 3) / 4 * 4;  // 16-byte row stride for TMA
+  auto al = [](size_t x) { return (x + 255) / 256 * 256; };
+  const size_t a_part = al(static_cast<size_t>(M) * Kp * 4);
+  const size_t b_part = al(static_cast<size_t>(N) * Kp * 4);
+  char* ws = static_cast<char*>(stream_workspace(s, 2 * a_part + 2 * b_part, 0, false));
+  if (!ws) return OJX_ERR_OOM;
+  float* a_hi = reinterpret_cast<float*>(ws);
+  float* a_lo = reinterpret_cast<float*>(ws + a_part);
+  float* b_hi = reinterpret_cast<float*>(ws + 2 * a_part);
+  float* b_lo = reinterpret_cast<float*>(ws + 2 * a_part + b_part);
+  // A -> [M][Kp]; op(B)^T -> [N][Kp] (the MMA's B operand is N x K, K-major).
+  dim3 blk(256);
+  split_tf32_kernel<<<dim3((Kp + 31) / 32, (M + 31) / 32), blk, 0, s>>>(
+      static_cast<const float*>(d.a), d.lda, d.trans_a ? 1 : 0, M, K, Kp, a_hi, a_lo);
+  g_launches.fetch_add(1);
+  split_tf32_kernel<<<dim3((Kp + 31) / 32, (N + 31) / 32), blk, 0, s>>>(
+      static_cast<const float*>(d.b), d.ldb, d.trans_b ? 0 : 1, N, K, Kp, b_hi, b_lo);
+  g_launches.fetch_add(1);
+  int st = cuda_status(cudaGetLastError(), "split_tf32 launch");
+  if (st) return st;
+  constexpr int BN = 128;
+  CUtensorMap ta, tb, ta2, tb2;
+  const auto F = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  if ((st = make_tmap_2d_sw128(&ta, F, 4, a_hi, Kp, M, Kp * 4ull, 32, 128))) return st;
+  if ((st = make_tmap_2d_sw128(&ta2, F, 4, a_lo, Kp, M, Kp * 4ull, 32, 128))) return st;
+  if ((st = make_tmap_2d_sw128(&tb, F, 4, b_hi, Kp, N, Kp * 4ull, 32, BN))) return st;
+  if ((st = make_tmap_2d_sw128(&tb2, F, 4, b_lo, Kp, N, Kp * 4ull, 32, BN))) return st;
+  return run_tc<1, 2, 0, 0, BN, 3>(ta, tb, ta2, tb2, make_epi(d), M, N, Kp, s);
+}
+
+}  // namespace ojx

@@ -1,0 +1,55 @@
+// internal.h — shared host-side declarations of libojx (not part of the C-ABI).
+#pragma once
+#include <cuda_runtime.h>
+#include <cstdint>
+#include <cstddef>
+#include <atomic>
+#include "../../include/ojx.h"
+
+namespace ojx {
+
+// Thread-local error message; returns `code` so call sites can `return set_error(...)`.
+int set_error(int code, const char* fmt, ...);
+// OJX_OK if e == cudaSuccess, else records the CUDA error string and returns OJX_ERR_CUDA
+// (OJX_ERR_OOM for cudaErrorMemoryAllocation).
+int cuda_status(cudaError_t e, const char* what);
+
+extern std::atomic<uint64_t> g_launches;   // kernels launched by this library
+extern std::atomic<uint64_t> g_wait_budget;  // SM cycles a device-side wait may spin
+extern std::atomic<int> g_silence_producer_once;
+void set_last_route(int route);
+
+struct DeviceProps {
+  int device = -1;
+  int sm_count = 0;
+  int max_smem_optin = 0;
+  int cc_major = 0, cc_minor = 0;
+};
+// Properties of the current device (cached per device).
+const DeviceProps& current_props();
+
+// Per-stream scratch buffers, grown on demand and kept for the life of the
+// process.  slot selects one of several independent buffers per stream.  With
+// `zero`, a freshly (re)allocated buffer is cleared on the stream.  Returns
+// nullptr and sets the error on failure.
+void* stream_workspace(cudaStream_t s, size_t bytes, int slot, bool zero);
+
+// Kernel families (implemented in the .cu files).
+int launch_tc_gemm(const ojx_gemm_desc& d, cudaStream_t s);
+int launch_tc_gemm_3xtf32(const ojx_gemm_desc& d, cudaStream_t s);
+int launch_skinny_gemm(const ojx_gemm_desc& d, cudaStream_t s);
+int launch_simt_gemm(const ojx_gemm_desc& d, cudaStream_t s);
+bool tc_gemm_supported(const ojx_gemm_desc& d);
+bool skinny_supported(const ojx_gemm_desc& d);
+
+int launch_elementwise(void* out, int dt_out, const void* a, int dt_a, const void* b, int dt_b,
+                       int bin, const int32_t* un, int n_un, int64_t n, cudaStream_t s);
+int launch_transpose(void* out, const void* in, int64_t rows, int64_t cols, int dtype,
+                     cudaStream_t s);
+int launch_fill(void* out, double v, int64_t n, int dtype, cudaStream_t s);
+int launch_cast(void* out, int dt_out, const void* in, int dt_in, int64_t n, cudaStream_t s);
+int read_and_clear_device_error(unsigned int* word);
+
+inline int dtype_size(int dt) { return dt == OJX_F32 ? 4 : 2; }
+
+}  // namespace ojx

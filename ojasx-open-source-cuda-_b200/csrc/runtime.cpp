@@ -1,0 +1,559 @@
+// runtime.cpp — the C-ABI of libojx: device/context, caching allocator, copies,
+// streams/events, error reporting and the GEMM route selection.
+//
+// Replaces torchcl/runtime/context.py (device + queue singletons),
+// torchcl/runtime/memory.py (CLBufferPool), torchcl/runtime/stream.py and the
+// kernel choice of torchcl/ops/engine.py:156-255.
+#include <cuda_runtime.h>
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+#include "internal.h"
+
+namespace ojx {
+
+static thread_local std::string t_last_error;
+static thread_local int t_last_route = OJX_ROUTE_NONE;
+std::atomic<uint64_t> g_launches{0};
+std::atomic<uint64_t> g_wait_budget{4000000000ull};  // about 2 s at B200 clocks
+std::atomic<int> g_silence_producer_once{0};
+
+int set_error(int code, const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_last_error = buf;
+  return code;
+}
+
+int cuda_status(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return OJX_OK;
+  const int code = e == cudaErrorMemoryAllocation ? OJX_ERR_OOM : OJX_ERR_CUDA;
+  set_error(code, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+  if (e == cudaErrorMemoryAllocation) (void)cudaGetLastError();  // not sticky; clear it
+  return code;
+}
+
+void set_last_route(int route) { t_last_route = route; }
+
+const DeviceProps& current_props() {
+  static std::mutex mu;
+  static DeviceProps props[128];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 128) dev = 0;
+  std::lock_guard<std::mutex> g(mu);
+  DeviceProps& p = props[dev];
+  if (p.device != dev) {
+    cudaDeviceGetAttribute(&p.sm_count, cudaDevAttrMultiProcessorCount, dev);
+    cudaDeviceGetAttribute(&p.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaDeviceGetAttribute(&p.cc_major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&p.cc_minor, cudaDevAttrComputeCapabilityMinor, dev);
+    p.device = dev;
+  }
+  return p;
+}
+
+// ── caching allocator ───────────────────────────────────────────────────────
+// Bins: 512 B minimum, powers of two up to 64 MiB (the slab policy of
+// torchcl/runtime/memory.py:20-24, with a floor that keeps every block 256-byte
+// aligned for TMA), and 2 MiB multiples above that so very large tensors do not
+// waste up to half their size.  A freed block goes back to its bin; an OOM frees
+// every cached block and retries once (memory.py:109-115).  Reuse is ordered on
+// the device only through the stream the caller uses for the block: like the
+// reference's single in-order queue, callers that hand a freed buffer to another
+// stream must synchronise first.
+class Pool {
+ public:
+  static size_t bin_size(size_t n) {
+    if (n <= 512) return 512;
+    if (n <= (size_t(64) << 20)) {
+      size_t b = 512;
+      while (b < n) b <<= 1;
+      return b;
+    }
+    const size_t g = size_t(2) << 20;
+    return (n + g - 1) / g * g;
+  }
+
+  int malloc(size_t n, void** out, size_t* cap) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const size_t c = bin_size(n);
+    std::lock_guard<std::mutex> g(mu_);
+    auto& bin = bins_[{dev, c}];
+    void* p = nullptr;
+    if (!bin.empty()) {
+      p = bin.back();
+      bin.pop_back();
+      st_.reuse_count++;
+      st_.cached_bytes -= static_cast<int64_t>(c);
+    } else {
+      cudaError_t e = raw_malloc(&p, c);
+      if (e == cudaErrorMemoryAllocation) {
+        (void)cudaGetLastError();
+        release_cached_locked();
+        st_.evictions++;
+        e = raw_malloc(&p, c);
+      }
+      if (e != cudaSuccess) {
+        (void)cudaGetLastError();
+        return set_error(e == cudaErrorMemoryAllocation ? OJX_ERR_OOM : OJX_ERR_CUDA,
+                         "ojx_malloc(%zu): %s after evicting the cache", n, cudaGetErrorString(e));
+      }
+      st_.alloc_count++;
+      st_.total_allocated_bytes += static_cast<int64_t>(c);
+    }
+    active_[p] = {dev, c};
+    st_.active_bytes += static_cast<int64_t>(c);
+    st_.active_buffers = static_cast<int64_t>(active_.size());
+    st_.peak_bytes = std::max(st_.peak_bytes, st_.active_bytes);
+    *out = p;
+    if (cap) *cap = c;
+    return OJX_OK;
+  }
+
+  int free(void* p) {
+    if (!p) return OJX_OK;
+    std::lock_guard<std::mutex> g(mu_);
+    auto it = active_.find(p);
+    if (it == active_.end()) return set_error(OJX_ERR_INVALID, "ojx_free(%p): not a live pool block", p);
+    const Block b = it->second;
+    active_.erase(it);
+    bins_[{b.dev, b.cap}].push_back(p);
+    st_.free_count++;
+    st_.active_bytes -= static_cast<int64_t>(b.cap);
+    st_.cached_bytes += static_cast<int64_t>(b.cap);
+    st_.active_buffers = static_cast<int64_t>(active_.size());
+    return OJX_OK;
+  }
+
+  int empty_cache() {
+    std::lock_guard<std::mutex> g(mu_);
+    return release_cached_locked();
+  }
+
+  void stats(ojx_pool_stats* out) {
+    std::lock_guard<std::mutex> g(mu_);
+    *out = st_;
+  }
+
+  void fail_next(int64_t n) {
+    std::lock_guard<std::mutex> g(mu_);
+    fail_next_ = n;
+  }
+
+ private:
+  struct Block {
+    int dev;
+    size_t cap;
+  };
+  cudaError_t raw_malloc(void** p, size_t n) {
+    if (fail_next_ > 0) {
+      --fail_next_;
+      return cudaErrorMemoryAllocation;
+    }
+    return cudaMalloc(p, n);
+  }
+  int release_cached_locked() {
+    int cur = 0;
+    cudaGetDevice(&cur);
+    int st = OJX_OK;
+    for (auto& kv : bins_) {
+      if (kv.second.empty()) continue;
+      cudaSetDevice(kv.first.first);
+      for (void* p : kv.second) {
+        const cudaError_t e = cudaFree(p);
+        if (e != cudaSuccess && st == OJX_OK) st = cuda_status(e, "cudaFree(cached block)");
+      }
+      kv.second.clear();
+    }
+    bins_.clear();
+    st_.cached_bytes = 0;
+    cudaSetDevice(cur);
+    return st;
+  }
+
+  std::mutex mu_;
+  std::map<std::pair<int, size_t>, std::vector<void*>> bins_;
+  std::unordered_map<void*, Block> active_;
+  ojx_pool_stats st_{};
+  int64_t fail_next_ = 0;
+};
+
+static Pool& pool() {
+  static Pool* p = new Pool();  // never destroyed: blocks may outlive static teardown
+  return *p;
+}
+
+// ── per-stream workspaces ───────────────────────────────────────────────────
+struct WsKey {
+  int dev;
+  cudaStream_t s;
+  int slot;
+  bool operator<(const WsKey& o) const {
+    if (dev != o.dev) return dev < o.dev;
+    if (s != o.s) return s < o.s;
+    return slot < o.slot;
+  }
+};
+struct WsBuf {
+  void* p = nullptr;
+  size_t bytes = 0;
+};
+
+void* stream_workspace(cudaStream_t s, size_t bytes, int slot, bool zero) {
+  static std::mutex mu;
+  static std::map<WsKey, WsBuf>* bufs = new std::map<WsKey, WsBuf>();
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> g(mu);
+  WsBuf& w = (*bufs)[{dev, s, slot}];
+  if (w.bytes >= bytes && w.p) return w.p;
+  if (w.p) {
+    // Growing: earlier launches on this stream may still read the old buffer.
+    if (cuda_status(cudaStreamSynchronize(s), "workspace grow: stream sync")) return nullptr;
+    cudaFree(w.p);
+    w = WsBuf{};
+  }
+  const size_t g2 = size_t(2) << 20;
+  const size_t nb = (std::max<size_t>(bytes, 1) + g2 - 1) / g2 * g2;
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, nb);
+  if (e == cudaErrorMemoryAllocation) {
+    (void)cudaGetLastError();
+    pool().empty_cache();
+    e = cudaMalloc(&p, nb);
+  }
+  if (e != cudaSuccess) {
+    cuda_status(e, "workspace cudaMalloc");
+    return nullptr;
+  }
+  if (zero && cuda_status(cudaMemsetAsync(p, 0, nb, s), "workspace clear")) {
+    cudaFree(p);
+    return nullptr;
+  }
+  w.p = p;
+  w.bytes = nb;
+  return p;
+}
+
+static bool valid_dtype(int dt) { return dt == OJX_F32 || dt == OJX_BF16 || dt == OJX_F16; }
+static bool valid_unary(int op) { return op >= OJX_UN_RELU && op <= OJX_UN_SQUARE; }
+static bool valid_binary(int op) { return op >= OJX_BIN_ADD && op <= OJX_BIN_DIV; }
+
+}  // namespace ojx
+
+using namespace ojx;
+
+extern "C" {
+
+int ojx_abi_version(void) { return OJX_ABI_VERSION; }
+
+int ojx_device_count(int* count) {
+  if (!count) return set_error(OJX_ERR_INVALID, "count is NULL");
+  int n = 0;
+  const cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();
+    *count = 0;
+    return cuda_status(e, "cudaGetDeviceCount");
+  }
+  *count = n;
+  return OJX_OK;
+}
+
+int ojx_init(int device, ojx_device_info* info) {
+  int n = 0;
+  int st = ojx_device_count(&n);
+  if (st) return st;
+  if (device < 0 || device >= n)
+    return set_error(OJX_ERR_INVALID, "device %d out of range (%d CUDA device(s))", device, n);
+  if ((st = cuda_status(cudaSetDevice(device), "cudaSetDevice"))) return st;
+  if ((st = cuda_status(cudaFree(nullptr), "context init"))) return st;
+  const DeviceProps& p = current_props();
+  if (p.cc_major < 10)
+    return set_error(OJX_ERR_UNSUPPORTED, "device %d is sm_%d%d; libojx is built for sm_100a", device,
+                     p.cc_major, p.cc_minor);
+  if (info) {
+    cudaDeviceProp prop;
+    if ((st = cuda_status(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties")))
+      return st;
+    std::memset(info, 0, sizeof(*info));
+    std::snprintf(info->name, sizeof(info->name), "%s", prop.name);
+    info->device = device;
+    info->cc_major = prop.major;
+    info->cc_minor = prop.minor;
+    info->sm_count = prop.multiProcessorCount;
+    info->total_mem_bytes = static_cast<int64_t>(prop.totalGlobalMem);
+    info->l2_bytes = prop.l2CacheSize;
+    info->max_smem_per_block = static_cast<int32_t>(prop.sharedMemPerBlockOptin);
+    int clk = 0;
+    cudaDeviceGetAttribute(&clk, cudaDevAttrClockRate, device);
+    info->clock_khz = clk;
+  }
+  return OJX_OK;
+}
+
+int ojx_current_device(int* device) {
+  if (!device) return set_error(OJX_ERR_INVALID, "device is NULL");
+  return cuda_status(cudaGetDevice(device), "cudaGetDevice");
+}
+
+int ojx_synchronize(void) { return cuda_status(cudaDeviceSynchronize(), "cudaDeviceSynchronize"); }
+
+const char* ojx_last_error(void) { return t_last_error.c_str(); }
+
+int ojx_poll_device_error(void) {
+  unsigned int w = 0;
+  int st = read_and_clear_device_error(&w);
+  if (st) return st;
+  if (w & 1u)  // bit 0: a bounded wait expired (sm100.cuh, OJX_DEVERR_TIMEOUT)
+    return set_error(OJX_ERR_TIMEOUT,
+                     "a device-side wait exceeded its budget; the kernel returned early and its "
+                     "output is incomplete");
+  return OJX_OK;
+}
+
+int ojx_set_wait_budget(uint64_t cycles) {
+  if (cycles == 0) return set_error(OJX_ERR_INVALID, "wait budget must be positive");
+  g_wait_budget.store(cycles);
+  return OJX_OK;
+}
+
+uint64_t ojx_kernel_launch_count(void) { return g_launches.load(); }
+
+int ojx_last_route(void) { return t_last_route; }
+
+int ojx_malloc(size_t nbytes, void** dptr, size_t* capacity) {
+  if (!dptr) return set_error(OJX_ERR_INVALID, "dptr is NULL");
+  return pool().malloc(nbytes, dptr, capacity);
+}
+
+int ojx_free(void* dptr) { return pool().free(dptr); }
+
+int ojx_empty_cache(void) { return pool().empty_cache(); }
+
+int ojx_pool_stats_get(ojx_pool_stats* out) {
+  if (!out) return set_error(OJX_ERR_INVALID, "out is NULL");
+  pool().stats(out);
+  return OJX_OK;
+}
+
+int ojx_pool_bin_size(size_t nbytes, size_t* capacity) {
+  if (!capacity) return set_error(OJX_ERR_INVALID, "capacity is NULL");
+  *capacity = Pool::bin_size(nbytes);
+  return OJX_OK;
+}
+
+int ojx_pool_debug_fail_next(int64_t n_allocs) {
+  pool().fail_next(n_allocs);
+  return OJX_OK;
+}
+
+static int copy(void* dst, const void* src, size_t n, ojx_stream s, const char* what) {
+  if (n == 0) return OJX_OK;
+  if (!dst || !src) return set_error(OJX_ERR_INVALID, "%s: NULL pointer", what);
+  return cuda_status(cudaMemcpyAsync(dst, src, n, cudaMemcpyDefault, static_cast<cudaStream_t>(s)),
+                     what);
+}
+
+int ojx_memcpy_h2d(void* dst, const void* src, size_t n, ojx_stream s) {
+  return copy(dst, src, n, s, "ojx_memcpy_h2d");
+}
+int ojx_memcpy_d2h(void* dst, const void* src, size_t n, ojx_stream s) {
+  return copy(dst, src, n, s, "ojx_memcpy_d2h");
+}
+int ojx_memcpy_d2d(void* dst, const void* src, size_t n, ojx_stream s) {
+  return copy(dst, src, n, s, "ojx_memcpy_d2d");
+}
+int ojx_memset(void* dst, int value, size_t n, ojx_stream s) {
+  if (n == 0) return OJX_OK;
+  if (!dst) return set_error(OJX_ERR_INVALID, "ojx_memset: NULL pointer");
+  return cuda_status(cudaMemsetAsync(dst, value, n, static_cast<cudaStream_t>(s)), "ojx_memset");
+}
+int ojx_host_alloc(size_t n, void** p) {
+  if (!p) return set_error(OJX_ERR_INVALID, "host_ptr is NULL");
+  return cuda_status(cudaHostAlloc(p, std::max<size_t>(n, 1), cudaHostAllocDefault), "cudaHostAlloc");
+}
+int ojx_host_free(void* p) { return cuda_status(cudaFreeHost(p), "cudaFreeHost"); }
+
+int ojx_stream_create(ojx_stream* s) {
+  if (!s) return set_error(OJX_ERR_INVALID, "s is NULL");
+  cudaStream_t cs;
+  int st = cuda_status(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking), "cudaStreamCreate");
+  if (!st) *s = cs;
+  return st;
+}
+int ojx_stream_destroy(ojx_stream s) {
+  return cuda_status(cudaStreamDestroy(static_cast<cudaStream_t>(s)), "cudaStreamDestroy");
+}
+int ojx_stream_synchronize(ojx_stream s) {
+  return cuda_status(cudaStreamSynchronize(static_cast<cudaStream_t>(s)), "cudaStreamSynchronize");
+}
+int ojx_stream_wait_event(ojx_stream s, ojx_event e) {
+  return cuda_status(
+      cudaStreamWaitEvent(static_cast<cudaStream_t>(s), static_cast<cudaEvent_t>(e), 0),
+      "cudaStreamWaitEvent");
+}
+int ojx_event_create(ojx_event* e, int enable_timing) {
+  if (!e) return set_error(OJX_ERR_INVALID, "e is NULL");
+  cudaEvent_t ev;
+  int st = cuda_status(
+      cudaEventCreateWithFlags(&ev, enable_timing ? cudaEventDefault : cudaEventDisableTiming),
+      "cudaEventCreate");
+  if (!st) *e = ev;
+  return st;
+}
+int ojx_event_destroy(ojx_event e) {
+  return cuda_status(cudaEventDestroy(static_cast<cudaEvent_t>(e)), "cudaEventDestroy");
+}
+int ojx_event_record(ojx_event e, ojx_stream s) {
+  return cuda_status(cudaEventRecord(static_cast<cudaEvent_t>(e), static_cast<cudaStream_t>(s)),
+                     "cudaEventRecord");
+}
+int ojx_event_query(ojx_event e, int* done) {
+  if (!done) return set_error(OJX_ERR_INVALID, "done is NULL");
+  const cudaError_t r = cudaEventQuery(static_cast<cudaEvent_t>(e));
+  if (r == cudaErrorNotReady) {
+    (void)cudaGetLastError();
+    *done = 0;
+    return OJX_OK;
+  }
+  *done = r == cudaSuccess;
+  return cuda_status(r, "cudaEventQuery");
+}
+int ojx_event_synchronize(ojx_event e) {
+  return cuda_status(cudaEventSynchronize(static_cast<cudaEvent_t>(e)), "cudaEventSynchronize");
+}
+int ojx_event_elapsed_ms(ojx_event a, ojx_event b, float* ms) {
+  if (!ms) return set_error(OJX_ERR_INVALID, "ms is NULL");
+  return cuda_status(
+      cudaEventElapsedTime(ms, static_cast<cudaEvent_t>(a), static_cast<cudaEvent_t>(b)),
+      "cudaEventElapsedTime");
+}
+
+int ojx_gemm(const ojx_gemm_desc* in, ojx_stream stream) {
+  set_last_route(OJX_ROUTE_NONE);
+  if (!in) return set_error(OJX_ERR_INVALID, "ojx_gemm: desc is NULL");
+  ojx_gemm_desc d = *in;
+  if (d.M < 0 || d.N < 0 || d.K < 0)
+    return set_error(OJX_ERR_INVALID, "ojx_gemm: negative dimension (%lld, %lld, %lld)",
+                     (long long)d.M, (long long)d.N, (long long)d.K);
+  if (!valid_dtype(d.dtype_a) || !valid_dtype(d.dtype_b) || !valid_dtype(d.dtype_c))
+    return set_error(OJX_ERR_INVALID, "ojx_gemm: unknown dtype");
+  if (d.n_unary < 0 || d.n_unary > OJX_MAX_UNARY)
+    return set_error(OJX_ERR_INVALID, "ojx_gemm: n_unary %d out of range", d.n_unary);
+  for (int i = 0; i < d.n_unary; ++i)
+    if (!valid_unary(d.unary[i]))
+      return set_error(OJX_ERR_INVALID, "ojx_gemm: unknown unary op %d", d.unary[i]);
+  if (d.operand_kind != OJX_OPERAND_NONE) {
+    if (d.operand_kind != OJX_OPERAND_ROW && d.operand_kind != OJX_OPERAND_FULL)
+      return set_error(OJX_ERR_INVALID, "ojx_gemm: unknown operand kind %d", d.operand_kind);
+    if (!d.operand) return set_error(OJX_ERR_INVALID, "ojx_gemm: operand pointer is NULL");
+    if (!valid_binary(d.binary_op))
+      return set_error(OJX_ERR_INVALID, "ojx_gemm: unknown binary op %d", d.binary_op);
+    if (!valid_dtype(d.dtype_operand))
+      return set_error(OJX_ERR_INVALID, "ojx_gemm: unknown operand dtype");
+  }
+  if (d.M == 0 || d.N == 0) return OJX_OK;
+  if (!d.c || (d.K > 0 && (!d.a || !d.b)))
+    return set_error(OJX_ERR_INVALID, "ojx_gemm: NULL matrix pointer");
+  if (d.lda == 0) d.lda = d.trans_a ? d.M : d.K;
+  if (d.ldb == 0) d.ldb = d.trans_b ? d.K : d.N;
+  if (d.ldc == 0) d.ldc = d.N;
+  if (d.ld_operand == 0) d.ld_operand = d.N;
+  if (d.lda < (d.trans_a ? d.M : d.K) || d.ldb < (d.trans_b ? d.K : d.N) || d.ldc < d.N ||
+      (d.operand_kind == OJX_OPERAND_FULL && d.ld_operand < d.N))
+    return set_error(OJX_ERR_INVALID, "ojx_gemm: leading dimension smaller than the row length");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const DeviceProps& p = current_props();
+  if (p.cc_major < 10)
+    return set_error(OJX_ERR_NOT_INITIALIZED, "ojx_gemm: current device is not sm_100 (call ojx_init)");
+
+  const bool f16 = d.dtype_a == d.dtype_b && (d.dtype_a == OJX_BF16 || d.dtype_a == OJX_F16);
+  const bool f32 = d.dtype_a == OJX_F32 && d.dtype_b == OJX_F32;
+  int route = OJX_ROUTE_SIMT;
+  if (!(d.flags & OJX_GEMM_FLAG_FORCE_SIMT) && d.K > 0) {
+    if (f16) {
+      const bool skinny_ok = !(d.flags & OJX_GEMM_FLAG_NO_SKINNY) && skinny_supported(d);
+      if (skinny_ok && (d.M <= 16 || (d.flags & OJX_GEMM_FLAG_FORCE_SKINNY)))
+        route = OJX_ROUTE_SKINNY;
+      else if (tc_gemm_supported(d))
+        route = OJX_ROUTE_TC_F16;
+    } else if (f32 && d.fp32_mode != OJX_FP32_FFMA && d.M <= INT32_MAX && d.N <= INT32_MAX &&
+               d.K <= INT32_MAX) {
+      if (d.fp32_mode == OJX_FP32_3XTF32 || d.M > 16) route = OJX_ROUTE_TC_3XTF32;
+    }
+  }
+  int st;
+  switch (route) {
+    case OJX_ROUTE_SKINNY: st = launch_skinny_gemm(d, s); break;
+    case OJX_ROUTE_TC_F16: st = launch_tc_gemm(d, s); break;
+    case OJX_ROUTE_TC_3XTF32: st = launch_tc_gemm_3xtf32(d, s); break;
+    default: st = launch_simt_gemm(d, s); break;
+  }
+  if (st == OJX_OK) set_last_route(route);
+  return st;
+}
+
+int ojx_elementwise(void* out, int32_t dtype_out, const void* a, int32_t dtype_a, const void* b,
+                    int32_t dtype_b, int32_t binary_op, const int32_t* unary, int32_t n_unary,
+                    int64_t n, ojx_stream s) {
+  if (n < 0) return set_error(OJX_ERR_INVALID, "ojx_elementwise: negative length");
+  if (n == 0) return OJX_OK;
+  if (!out || !a) return set_error(OJX_ERR_INVALID, "ojx_elementwise: NULL pointer");
+  if (!valid_dtype(dtype_out) || !valid_dtype(dtype_a) || (b && !valid_dtype(dtype_b)))
+    return set_error(OJX_ERR_INVALID, "ojx_elementwise: unknown dtype");
+  if (b && !valid_binary(binary_op))
+    return set_error(OJX_ERR_INVALID, "ojx_elementwise: unknown binary op %d", binary_op);
+  if (n_unary < 0 || n_unary > OJX_MAX_UNARY || (n_unary > 0 && !unary))
+    return set_error(OJX_ERR_INVALID, "ojx_elementwise: bad unary chain");
+  for (int i = 0; i < n_unary; ++i)
+    if (!valid_unary(unary[i]))
+      return set_error(OJX_ERR_INVALID, "ojx_elementwise: unknown unary op %d", unary[i]);
+  return launch_elementwise(out, dtype_out, a, dtype_a, b, dtype_b, binary_op, unary, n_unary, n,
+                            static_cast<cudaStream_t>(s));
+}
+
+int ojx_transpose(void* out, const void* in, int64_t rows, int64_t cols, int32_t dtype,
+                  ojx_stream s) {
+  if (rows < 0 || cols < 0) return set_error(OJX_ERR_INVALID, "ojx_transpose: negative shape");
+  if (rows * cols == 0) return OJX_OK;
+  if (!out || !in) return set_error(OJX_ERR_INVALID, "ojx_transpose: NULL pointer");
+  if (!valid_dtype(dtype)) return set_error(OJX_ERR_INVALID, "ojx_transpose: unknown dtype");
+  return launch_transpose(out, in, rows, cols, dtype, static_cast<cudaStream_t>(s));
+}
+
+int ojx_fill(void* out, double value, int64_t n, int32_t dtype, ojx_stream s) {
+  if (n < 0) return set_error(OJX_ERR_INVALID, "ojx_fill: negative length");
+  if (n == 0) return OJX_OK;
+  if (!out) return set_error(OJX_ERR_INVALID, "ojx_fill: NULL pointer");
+  if (!valid_dtype(dtype)) return set_error(OJX_ERR_INVALID, "ojx_fill: unknown dtype");
+  return launch_fill(out, value, n, dtype, static_cast<cudaStream_t>(s));
+}
+
+int ojx_cast(void* out, int32_t dtype_out, const void* in, int32_t dtype_in, int64_t n,
+             ojx_stream s) {
+  if (n < 0) return set_error(OJX_ERR_INVALID, "ojx_cast: negative length");
+  if (n == 0) return OJX_OK;
+  if (!out || !in) return set_error(OJX_ERR_INVALID, "ojx_cast: NULL pointer");
+  if (!valid_dtype(dtype_out) || !valid_dtype(dtype_in))
+    return set_error(OJX_ERR_INVALID, "ojx_cast: unknown dtype");
+  return launch_cast(out, dtype_out, in, dtype_in, n, static_cast<cudaStream_t>(s));
+}
+
+int ojx_debug_silence_producer_once(void) {
+  g_silence_producer_once.store(1);
+  return OJX_OK;
+}
+
+}  // extern "C"

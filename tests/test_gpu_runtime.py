@@ -1,0 +1,102 @@
+"""Runtime layer on the device: caching pool statistics and evict-and-retry under
+an injected cudaMalloc failure, the bounded-wait timeout path (no GPU fault: the
+producer warp is silenced so the consumer's bounded wait expires and the kernel
+returns), and kernel-launch accounting."""
+import ctypes
+
+import pytest
+import torch
+
+import torchcl
+from torchcl import _lib as L
+from torchcl.runtime.memory import get_buffer_pool
+
+from gpu_helpers import assert_half_parity, oracle_gemm, randn, run_gemm
+
+pytestmark = pytest.mark.gpu
+
+
+def test_pool_reuse_and_stats():
+    torchcl.init_opencl()
+    pool = get_buffer_pool()
+    s0 = pool.get_stats()
+    a = pool.allocate(3000)
+    assert a.capacity == 4096 and a.buffer % 256 == 0
+    pool.free(a)
+    b = pool.allocate(2500)  # same bin -> the freed block comes back
+    assert b.buffer == a.buffer
+    s1 = pool.get_stats()
+    assert s1["reuse_count"] >= s0["reuse_count"] + 1
+    assert s1["active_bytes"] - s0["active_bytes"] == 4096
+    pool.free(b)
+    assert pool.get_stats()["cached_bytes"] >= 4096
+
+
+def test_pool_evict_and_retry_then_oom():
+    torchcl.init_opencl()
+    pool = get_buffer_pool()
+    lib = L.lib()
+    cached = pool.allocate(1 << 20)
+    pool.free(cached)  # something to evict
+    ev0 = pool.get_stats()["evictions"]
+    lib.ojx_pool_debug_fail_next(1)  # first cudaMalloc fails, the retry after eviction succeeds
+    buf = pool.allocate(3 << 20)
+    assert pool.get_stats()["evictions"] == ev0 + 1
+    pool.free(buf)
+    lib.ojx_pool_debug_fail_next(2)  # both attempts fail -> MemoryError, like memory.py:111-115
+    with pytest.raises(MemoryError):
+        pool.allocate(5 << 20)
+    lib.ojx_pool_debug_fail_next(0)
+    ok = pool.allocate(5 << 20)  # the pool is usable afterwards
+    pool.free(ok)
+
+
+def test_bounded_wait_times_out_and_context_survives():
+    torchcl.init_opencl()
+    lib = L.lib()
+    M, N, K = 256, 256, 256
+    A = randn(1, (M, K), torch.bfloat16)
+    B = randn(2, (K, N), torch.bfloat16)
+    L.check(lib.ojx_poll_device_error())
+    lib.ojx_set_wait_budget(2_000_000)  # about a millisecond
+    try:
+        lib.ojx_debug_silence_producer_once()
+        C, route = run_gemm(A, B, flags=0x2)
+        assert route == "tc_f16"
+        with pytest.raises(L.TimeoutError_):
+            L.check(lib.ojx_poll_device_error())
+    finally:
+        lib.ojx_set_wait_budget(4_000_000_000)
+    # the same context keeps working
+    C, route = run_gemm(A, B, flags=0x2)
+    assert_half_parity(C.float().numpy(), oracle_gemm(A, B), tol=4e-3)
+    L.check(lib.ojx_poll_device_error())
+
+
+def test_skinny_timeout_path():
+    torchcl.init_opencl()
+    lib = L.lib()
+    X = randn(3, (4, 512), torch.bfloat16)
+    W = randn(4, (512, 1024), torch.bfloat16)
+    lib.ojx_set_wait_budget(2_000_000)
+    try:
+        lib.ojx_debug_silence_producer_once()
+        _, route = run_gemm(X, W)
+        assert route == "skinny"
+        with pytest.raises(L.TimeoutError_):
+            L.check(lib.ojx_poll_device_error())
+    finally:
+        lib.ojx_set_wait_budget(4_000_000_000)
+    C, _ = run_gemm(X, W)
+    assert_half_parity(C.float().numpy(), oracle_gemm(X, W), tol=4e-3)
+
+
+def test_launch_counter_and_device_info():
+    info = torchcl.get_device_info()
+    assert info["max_compute_units"] >= 100 and "sm_10" in info["version"]
+    lib = L.lib()
+    n0 = lib.ojx_kernel_launch_count()
+    A = randn(5, (128, 64), torch.bfloat16)
+    B = randn(6, (64, 128), torch.bfloat16)
+    run_gemm(A, B, flags=0x2)
+    assert lib.ojx_kernel_launch_count() == n0 + 1
