@@ -34,7 +34,9 @@ def test_tc_half_layouts(dtype, ta, tb, shape):
     M, N, K = shape
     A, B = _operands(sum(shape), M, N, K, dtype, ta, tb)
     C, route = run_gemm(A, B, trans_a=ta, trans_b=tb, flags=0x2)  # no skinny route
-    assert route == "tc_f16"
+    # TMA needs 16-byte row strides: lda = M (A stored transposed) or K, ldb = K or N
+    lda, ldb = (M if ta else K), (K if tb else N)
+    assert route == ("tc_f16" if lda % 8 == 0 and ldb % 8 == 0 else "simt")
     ref = oracle_gemm(A, B, trans_a=ta, trans_b=tb)
     assert_half_parity(C.float().numpy(), ref, tol=4e-3)
 
