@@ -67,7 +67,9 @@ __device__ __forceinline__ void store_elem(void* p, int64_t i, int dtype, float 
   }
 }
 
-// Everything a GEMM epilogue needs, passed by value as a kernel parameter.
+// Everything a GEMM epilogue needs, passed by value as a kernel parameter.  The
+// unary chain is packed 4 bits per op (op i in bits 4i..4i+3) so that reading it
+// never goes through local memory.
 struct EpiParams {
   void* c;
   int64_t ldc;
@@ -79,13 +81,17 @@ struct EpiParams {
   int32_t binary_op;
   int32_t operand_is_lhs;
   int32_t n_unary;
-  int32_t unary[OJX_MAX_UNARY];
+  uint32_t unary_packed;
 };
 
 // Host: copy the epilogue fields of a GEMM descriptor.
 EpiParams make_epi(const ojx_gemm_desc& d);
 
-// v = epilogue(acc) for output element (row, col); the caller checks bounds.
+__device__ __forceinline__ int unary_at(uint32_t packed, int i) {
+  return static_cast<int>((packed >> (4 * i)) & 15u);
+}
+
+// v = epilogue(acc) for one output element (row, col); the caller checks bounds.
 __device__ __forceinline__ float epilogue_value(const EpiParams& ep, float acc, int64_t row,
                                                 int64_t col) {
   float v = acc;
@@ -94,8 +100,102 @@ __device__ __forceinline__ float epilogue_value(const EpiParams& ep, float acc, 
     const float x = load_elem(ep.operand, idx, ep.dtype_operand);
     v = ep.operand_is_lhs ? apply_binary(ep.binary_op, x, v) : apply_binary(ep.binary_op, v, x);
   }
-  for (int i = 0; i < ep.n_unary; ++i) v = apply_unary(ep.unary[i], v);
+  for (int i = 0; i < ep.n_unary; ++i) v = apply_unary(unary_at(ep.unary_packed, i), v);
   return v;
+}
+
+// ── 16-wide variants: one dispatch per 16 consecutive columns of a row ─────────
+
+// x[0..15] = p[i0 .. i0+15] (only the first `valid` when the row ends early).
+__device__ __forceinline__ void load16(const void* p, int dtype, int64_t i0, int valid,
+                                       float (&x)[16]) {
+  const int esz = dtype == OJX_F32 ? 4 : 2;
+  const char* src = static_cast<const char*>(p) + i0 * esz;
+  if (valid == 16 && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+    if (dtype == OJX_F32) {
+      const float4* s4 = reinterpret_cast<const float4*>(src);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float4 f = __ldg(s4 + j);
+        x[4 * j] = f.x; x[4 * j + 1] = f.y; x[4 * j + 2] = f.z; x[4 * j + 3] = f.w;
+      }
+    } else {
+      const uint4* s4 = reinterpret_cast<const uint4*>(src);
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const uint4 u = __ldg(s4 + j);
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          if (dtype == OJX_BF16) {
+            const __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&w[k]);
+            x[8 * j + 2 * k] = __low2float(h);
+            x[8 * j + 2 * k + 1] = __high2float(h);
+          } else {
+            const __half2 h = *reinterpret_cast<const __half2*>(&w[k]);
+            x[8 * j + 2 * k] = __low2float(h);
+            x[8 * j + 2 * k + 1] = __high2float(h);
+          }
+        }
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) x[j] = j < valid ? load_elem(p, i0 + j, dtype) : 0.0f;
+  }
+}
+
+__device__ __forceinline__ void unary16(int op, float (&v)[16]) {
+#define OJX_U16(EXPR)                                         \
+  _Pragma("unroll") for (int j = 0; j < 16; ++j) {            \
+    const float x = v[j];                                     \
+    v[j] = (EXPR);                                            \
+  }                                                           \
+  break;
+  switch (op) {
+    case OJX_UN_RELU: OJX_U16(fmaxf(x, 0.0f))
+    case OJX_UN_SIGMOID: OJX_U16(__fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x))))
+    case OJX_UN_TANH: OJX_U16(tanhf(x))
+    case OJX_UN_NEG: OJX_U16(-x)
+    case OJX_UN_ABS: OJX_U16(fabsf(x))
+    case OJX_UN_EXP: OJX_U16(expf(x))
+    case OJX_UN_LOG: OJX_U16(logf(x))
+    case OJX_UN_SQRT: OJX_U16(__fsqrt_rn(x))
+    case OJX_UN_SILU: OJX_U16(__fdiv_rn(x, __fadd_rn(1.0f, expf(-x))))
+    case OJX_UN_GELU: OJX_U16(apply_unary(OJX_UN_GELU, x))
+    case OJX_UN_SQUARE: OJX_U16(__fmul_rn(x, x))
+    default: break;
+  }
+#undef OJX_U16
+}
+
+__device__ __forceinline__ void binary16(int op, bool lhs, float (&v)[16], const float (&x)[16]) {
+#define OJX_B16(EXPR)                                         \
+  _Pragma("unroll") for (int j = 0; j < 16; ++j) {            \
+    const float a = lhs ? x[j] : v[j], b = lhs ? v[j] : x[j]; \
+    v[j] = (EXPR);                                            \
+  }                                                           \
+  break;
+  switch (op) {
+    case OJX_BIN_ADD: OJX_B16(__fadd_rn(a, b))
+    case OJX_BIN_SUB: OJX_B16(__fsub_rn(a, b))
+    case OJX_BIN_MUL: OJX_B16(__fmul_rn(a, b))
+    case OJX_BIN_DIV: OJX_B16(__fdiv_rn(a, b))
+    default: break;
+  }
+#undef OJX_B16
+}
+
+// Epilogue of 16 consecutive columns col0.. of one row (valid = columns < N).
+__device__ __forceinline__ void epilogue16(const EpiParams& ep, float (&v)[16], int64_t row,
+                                           int64_t col0, int valid) {
+  if (ep.operand_kind != OJX_OPERAND_NONE) {
+    float x[16];
+    const int64_t i0 = ep.operand_kind == OJX_OPERAND_ROW ? col0 : row * ep.ld_operand + col0;
+    load16(ep.operand, ep.dtype_operand, i0, valid, x);
+    binary16(ep.binary_op, ep.operand_is_lhs != 0, v, x);
+  }
+  for (int i = 0; i < ep.n_unary; ++i) unary16(unary_at(ep.unary_packed, i), v);
 }
 
 }  // namespace ojx

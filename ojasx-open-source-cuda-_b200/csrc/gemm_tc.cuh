@@ -5,11 +5,12 @@
 // 297-343, 422-463) and the JIT's second elementwise launch
 // (torchcl/jit/compiler.py:99-133): C = epilogue(A·B) in one launch, one store.
 //
-// CTA = 192 threads, one CTA per SM, grid = min(#tiles, #SMs), tiles walked with a
+// CTA = 320 threads, one CTA per SM, grid = min(#tiles, #SMs), tiles walked with a
 // stride of gridDim.x in a grouped (8 M-blocks) raster for L2 reuse.
 //   warp 0      TMA producer: STAGES-deep ring of 128B-swizzled A/B tiles
 //   warp 1      TMEM owner + single-thread tcgen05.mma issuer
-//   warps 2..5  epilogue: TMEM -> registers -> bias/binary/unary chain -> store
+//   warps 2..9  epilogue: TMEM -> registers -> bias/binary/unary chain -> store;
+//               warp w reads TMEM lane quarter w%4, half (w-2)/4 of the columns
 // The accumulator is double-buffered in TMEM (2 x BN fp32 columns), so the
 // epilogue of tile i overlaps the MMAs of tile i+1.
 //
@@ -29,7 +30,8 @@
 namespace ojx {
 
 constexpr int TC_BM = 128;
-constexpr int TC_THREADS = 192;
+constexpr int TC_THREADS = 320;  // 2 control warps + 8 epilogue warps
+constexpr int TC_EPI_WARPS = 8;
 
 template <int KIND, int BN, int STAGES>
 struct TcLayout {
@@ -85,15 +87,13 @@ __device__ __forceinline__ void load_operand(uint32_t dst, const CUtensorMap* ma
 __device__ __forceinline__ void store_row16(const EpiParams& ep, const uint32_t (&r)[16],
                                             int64_t row, int col0, int N) {
   float v[16];
-  const bool full = col0 + 16 <= N;
+  const int valid = min(16, N - col0);
 #pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    v[j] = __uint_as_float(r[j]);
-    if (full || col0 + j < N) v[j] = epilogue_value(ep, v[j], row, col0 + j);
-  }
+  for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
+  epilogue16(ep, v, row, col0, valid);
   const int esz = ep.dtype_c == OJX_F32 ? 4 : 2;
   char* dst = static_cast<char*>(ep.c) + (row * ep.ldc + col0) * esz;
-  if (full && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+  if (valid == 16 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
     if (ep.dtype_c == OJX_F32) {
       float4* d4 = reinterpret_cast<float4*>(dst);
 #pragma unroll
@@ -117,7 +117,7 @@ __device__ __forceinline__ void store_row16(const EpiParams& ep, const uint32_t 
   } else {
 #pragma unroll
     for (int j = 0; j < 16; ++j)
-      if (col0 + j < N) store_elem(ep.c, row * ep.ldc + col0 + j, ep.dtype_c, v[j]);
+      if (j < valid) store_elem(ep.c, row * ep.ldc + col0 + j, ep.dtype_c, v[j]);
   }
 }
 
@@ -153,7 +153,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(tfull_bar(a), 1);
-      mbar_init(tempty_bar(a), 4);
+      mbar_init(tempty_bar(a), TC_EPI_WARPS);
     }
     mbar_init(done_bar, 1);
     *s_abort = 0;
@@ -270,8 +270,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
     __syncwarp();
   } else {
-    // ── epilogue warps 2..5: warp w reads TMEM lanes 32*(w%4) .. +31 ───────
+    // ── epilogue warps 2..9: lane quarter warp%4, column half (warp-2)/4 ──────
     const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -280,17 +281,21 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       int mb, nb;
       tile_coords(tile, tiles_m, tiles_n, mb, nb);
       const int64_t row = static_cast<int64_t>(mb) * TC_BM + q * 32 + lane;
-      const int n0 = nb * BN;
-      const uint32_t tbase =
-          tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      const int n0 = nb * BN + half * (BN / 2);
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                             static_cast<uint32_t>(acc * BN + half * (BN / 2));
 #pragma unroll 1
-      for (int c = 0; c < BN / 16; ++c) {
-        const int col0 = n0 + c * 16;
+      for (int c = 0; c < BN / 2; c += 32) {
+        const int col0 = n0 + c;
         if (col0 >= N) break;  // uniform across the warp
-        uint32_t r[16];
-        tmem_ld16(tbase + c * 16, r);
+        uint32_t r0[16], r1[16];
+        tmem_ld16(tbase + c, r0);
+        tmem_ld16(tbase + c + 16, r1);
         tmem_wait_ld();
-        if (row < M) store_row16(ep, r, row, col0, N);
+        if (row < M) {
+          store_row16(ep, r0, row, col0, N);
+          if (col0 + 16 < N) store_row16(ep, r1, row, col0 + 16, N);
+        }
       }
       tc_fence_before();
       __syncwarp();
@@ -368,7 +373,9 @@ EpiParams make_epi(const ojx_gemm_desc& d) {
   ep.binary_op = d.binary_op;
   ep.operand_is_lhs = d.operand_is_lhs;
   ep.n_unary = d.n_unary;
-  for (int i = 0; i < OJX_MAX_UNARY; ++i) ep.unary[i] = i < d.n_unary ? d.unary[i] : 0;
+  ep.unary_packed = 0;
+  for (int i = 0; i < d.n_unary && i < OJX_MAX_UNARY; ++i)
+    ep.unary_packed |= (static_cast<uint32_t>(d.unary[i]) & 15u) << (4 * i);
   return ep;
 }
 

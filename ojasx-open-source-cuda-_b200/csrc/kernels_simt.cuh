@@ -110,7 +110,7 @@ int launch_simt_gemm(const ojx_gemm_desc& d, cudaStream_t s) {
 struct EwParams {
   int32_t bin;
   int32_t n_un;
-  int32_t un[OJX_MAX_UNARY];
+  uint32_t un_packed;  // 4 bits per unary op
 };
 
 __global__ void __launch_bounds__(256)
@@ -120,7 +120,7 @@ __global__ void __launch_bounds__(256)
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
     float v = load_elem(a, i, dt_a);
     if (b) v = apply_binary(p.bin, v, load_elem(b, i, dt_b));
-    for (int k = 0; k < p.n_un; ++k) v = apply_unary(p.un[k], v);
+    for (int k = 0; k < p.n_un; ++k) v = apply_unary(unary_at(p.un_packed, k), v);
     store_elem(out, i, dt_out, v);
   }
 }
@@ -137,7 +137,7 @@ int launch_elementwise(void* out, int dt_out, const void* a, int dt_a, const voi
   EwParams p{};
   p.bin = bin;
   p.n_un = n_un;
-  for (int i = 0; i < n_un; ++i) p.un[i] = un[i];
+  for (int i = 0; i < n_un; ++i) p.un_packed |= (static_cast<uint32_t>(un[i]) & 15u) << (4 * i);
   elementwise_kernel<<<grid_for(n), 256, 0, s>>>(out, dt_out, a, dt_a, b, dt_b, p, n);
   g_launches.fetch_add(1);
   return cuda_status(cudaGetLastError(), "elementwise launch");
