@@ -1,23 +1,26 @@
-// gemm_skinny.cu — decode-shaped GEMM (M <= 16 rows of X) that streams W from HBM.
+// gemm_skinny.cuh — decode-shaped GEMM (M <= 16 rows of X) that streams W from HBM.
 //
 // The reference sends M < 32 to matmul_naive_f32 / matmul_bias_f32
 // (torchcl/kernels/matmul.cl:346-385 via engine.py:166-179): one work-item per
 // output element reading a whole column of B.  Here the GEMM is transposed so
-// the weight tile is the 128-wide tcgen05 operand:
+// the weight is the 128-row tcgen05 operand:
 //     C^T[n, m] = sum_k W^T[n, k] * X^T[k, m]      (MMA M = 128 columns of C,
 //                                                   MMA N = 16 padded rows of X)
-// and the K dimension is split "stream-K" style: the U = ceil(N/128) * ceil(K/64)
-// (tile, k-block) units are divided evenly over a persistent grid of one CTA per
-// SM, so every SM streams the same number of W bytes.  A CTA's units form at most
-// a few segments (consecutive k-blocks of one column tile).  A segment that covers
-// its whole tile is finished directly; otherwise each contributor writes its fp32
-// partial into a scratch slot and bumps the tile's arrival counter, and the CTA
-// that arrives last sums the partials in contributor order (deterministic) and
-// runs the fused epilogue.  No CTA ever waits on another.
+// Work is cut into units of (column group g = SK_TPU tiles of 128 columns, one
+// 64-deep k block): 32 KB of W and 8 MMAs per unit, so the per-unit
+// synchronisation (barrier wait, fence, commit) stays small next to the data.
+// The U = groups * k_blocks units are divided evenly ("stream-K") over a
+// persistent grid of one CTA per SM, so every SM streams the same number of W
+// bytes.  A CTA's units form at most a few segments (consecutive k blocks of one
+// group).  A segment that covers its whole group is finished directly; otherwise
+// each contributor writes its fp32 partial into a scratch slot and bumps the
+// group's arrival counter, and the CTA that arrives last sums the partials in
+// contributor order (deterministic) and runs the fused epilogue.  No CTA ever
+// waits on another.
 //
-// Scratch per call: partial slots  ceil(N/128) * max_contributors * 16 * 128 fp32,
-// and one 64-bit arrival counter per column tile holding (launch epoch << 32 | count)
-// so stale counts from an earlier launch never need resetting.
+// Scratch per call: partial slots  groups * max_contributors * SK_TPU*16*128 fp32,
+// and one 64-bit arrival counter per group holding (launch epoch << 32 | count),
+// so stale counts from an earlier (or aborted) launch never need resetting.
 #include <cuda_runtime.h>
 #include <algorithm>
 #include "sm100.cuh"
@@ -27,23 +30,28 @@
 
 namespace ojx {
 
-constexpr int SK_BN = 128;  // columns of C per tile (MMA M)
-constexpr int SK_MN = 16;   // padded rows of X (MMA N)
-constexpr int SK_BK = 64;   // k per unit (one 128-byte swizzle row of bf16)
-constexpr int SK_STAGES = 8;
+constexpr int SK_BN = 128;   // columns of C per tile (MMA M)
+constexpr int SK_TPU = 2;    // tiles per unit
+constexpr int SK_MN = 16;    // padded rows of X (MMA N)
+constexpr int SK_BK = 64;    // k per unit (one 128-byte swizzle row of bf16)
+constexpr int SK_STAGES = 6;
 constexpr int SK_THREADS = 192;
-constexpr int SK_W_BYTES = SK_BN * 128;
+constexpr int SK_W_BYTES = SK_TPU * SK_BN * 128;
 constexpr int SK_X_BYTES = SK_MN * 128;
 constexpr int SK_STAGE_BYTES = SK_W_BYTES + SK_X_BYTES;
-constexpr int SK_SMEM = SK_STAGES * SK_STAGE_BYTES + 256 + 1024;
+constexpr int SK_NBUF = 4;  // TMEM accumulator buffers (segments in flight)
+constexpr uint32_t SK_TMEM_COLS = SK_NBUF * SK_TPU * SK_MN;
+constexpr int SK_SLOT = SK_TPU * SK_MN * SK_BN;  // floats per partial slot
+constexpr int SK_SMEM = SK_STAGES * SK_STAGE_BYTES + 512 + 1024;
 static_assert(SK_STAGE_BYTES % 1024 == 0, "stage alignment");
+static_assert(SK_TMEM_COLS >= 32 && (SK_TMEM_COLS & (SK_TMEM_COLS - 1)) == 0, "TMEM alloc size");
 
 struct SkinnyParams {
   int M, N, K;
-  int n_tiles, KB;
+  int n_groups, KB;
   long long U;  // total units
   int G;        // CTAs
-  int maxc;     // partial slots per tile
+  int maxc;     // partial slots per group
   float* partials;
   unsigned long long* counters;
   unsigned int epoch;
@@ -71,9 +79,11 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SK_STAGES * SK_STAGE_BYTES);
-  volatile int* s_abort = reinterpret_cast<volatile int*>(bars + 2 * SK_STAGES + 5);
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 2 * SK_STAGES + 6);
-  volatile int* s_last = reinterpret_cast<volatile int*>(bars + 2 * SK_STAGES + 7);
+  constexpr int NB = 2 * SK_STAGES + 2 * SK_NBUF + 1;  // full, empty, tfull, tempty, done
+  volatile int* s_abort = reinterpret_cast<volatile int*>(bars + NB);
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + NB + 1);
+  volatile int* s_last = reinterpret_cast<volatile int*>(bars + NB + 2);
+  static_assert((NB + 3) * 8 <= 512, "barrier area");
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t sbase = smem_u32(smem);
@@ -81,15 +91,15 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
   auto full_bar = [&](int s) { return bar0 + 8u * s; };
   auto empty_bar = [&](int s) { return bar0 + 8u * (SK_STAGES + s); };
   auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * SK_STAGES + a); };
-  auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * SK_STAGES + 2 + a); };
-  const uint32_t done_bar = bar0 + 8u * (2 * SK_STAGES + 4);
+  auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * SK_STAGES + SK_NBUF + a); };
+  const uint32_t done_bar = bar0 + 8u * (2 * SK_STAGES + 2 * SK_NBUF);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < SK_STAGES; ++s) {
       mbar_init(full_bar(s), 1);
       mbar_init(empty_bar(s), 1);
     }
-    for (int a = 0; a < 2; ++a) {
+    for (int a = 0; a < SK_NBUF; ++a) {
       mbar_init(tfull_bar(a), 1);
       mbar_init(tempty_bar(a), 4);
     }
@@ -102,7 +112,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
     tma_prefetch_desc(&tmX);
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(s_tmem), 32);
+    tmem_alloc(smem_u32(s_tmem), SK_TMEM_COLS);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -112,23 +122,29 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
 
   const long long ub = unit_begin(blockIdx.x, p);
   const long long ue = unit_begin(blockIdx.x + 1, p);
+  const int g_begin = static_cast<int>(ub / p.KB);
+  const int kb_begin = static_cast<int>(ub - static_cast<long long>(g_begin) * p.KB);
+  const int n_units = static_cast<int>(ue - ub);
 
   if (warp == 0) {
+    // ── TMA producer ────────────────────────────────────────────────────
     if (lane == 0 && !p.silence_producer) {
-      int stage = 0;
+      int stage = 0, g = g_begin, kb = kb_begin;
       uint32_t phase = 0, issued = 0, issued_parity = 0;
-      for (long long u = ub; u < ue; ++u) {
-        const int t = static_cast<int>(u / p.KB), kb = static_cast<int>(u % p.KB);
+      for (int i = 0; i < n_units; ++i) {
         if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.budget, s_abort)) break;
         const uint32_t fb = full_bar(stage);
         mbar_arrive_expect_tx(fb, SK_STAGE_BYTES);
         const uint32_t sW = sbase + stage * SK_STAGE_BYTES;
-        const int n0 = t * SK_BN, k0 = kb * SK_BK;
-        if (W_MN) {
-          tma_load_2d(sW, &tmW, fb, n0, k0);
-          tma_load_2d(sW + 64 * 128, &tmW, fb, n0 + 64, k0);
-        } else {
-          tma_load_2d(sW, &tmW, fb, k0, n0);
+        const int n0 = g * (SK_TPU * SK_BN), k0 = kb * SK_BK;
+#pragma unroll
+        for (int j = 0; j < SK_TPU; ++j) {
+          if (W_MN) {
+            tma_load_2d(sW + j * (SK_BN * 128), &tmW, fb, n0 + j * SK_BN, k0);
+            tma_load_2d(sW + j * (SK_BN * 128) + 64 * 128, &tmW, fb, n0 + j * SK_BN + 64, k0);
+          } else {
+            tma_load_2d(sW + j * (SK_BN * 128), &tmW, fb, k0, n0 + j * SK_BN);
+          }
         }
         tma_load_2d(sW + SK_W_BYTES, &tmX, fb, k0, 0);
         issued |= 1u << stage;
@@ -137,105 +153,132 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
           stage = 0;
           phase ^= 1u;
         }
+        if (++kb == p.KB) {
+          kb = 0;
+          ++g;
+        }
       }
       for (int s = 0; s < SK_STAGES; ++s)
         if ((issued >> s) & 1u) mbar_wait_drain(full_bar(s), (issued_parity >> s) & 1u, p.budget);
     }
   } else if (warp == 1) {
+    // ── MMA issuer ──────────────────────────────────────────────────────
     if (lane == 0) {
       constexpr uint32_t IDESC = make_idesc(FMT, W_MN, 0, SK_BN, SK_MN);
-      int stage = 0, acc = 0;
+      int stage = 0, acc = 0, kb = kb_begin;
       uint32_t phase = 0, acc_phase = 0;
-      bool seg_open = false;
-      for (long long u = ub; u < ue; ++u) {
-        const bool seg_start = (u == ub) || (u % p.KB == 0);
-        const bool seg_end = (u + 1 == ue) || ((u + 1) % p.KB == 0);
+      bool seg_start = true;
+      for (int i = 0; i < n_units; ++i) {
+        const bool seg_end = (i + 1 == n_units) || (kb + 1 == p.KB);
         if (seg_start) {
           if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, p.budget, s_abort)) break;
           tc_fence_after();
-          seg_open = true;
         }
         if (!mbar_wait(full_bar(stage), phase, p.budget, s_abort)) break;
         tc_fence_after();
         const uint32_t sW = sbase + stage * SK_STAGE_BYTES;
-        const uint32_t sX = sW + SK_W_BYTES;
-        const uint32_t d = tmem_base + static_cast<uint32_t>(acc * SK_MN);
+        const uint64_t bd0 = make_sw128_desc(sW + SK_W_BYTES, 16, 1024);
+        const uint32_t d = tmem_base + static_cast<uint32_t>(acc * SK_TPU * SK_MN);
 #pragma unroll
-        for (int ks = 0; ks < 4; ++ks) {
-          const uint64_t ad = W_MN ? make_sw128_desc(sW + ks * 2048, 64 * 128, 1024)
-                                   : make_sw128_desc(sW + ks * 32, 16, 1024);
-          const uint64_t bd = make_sw128_desc(sX + ks * 32, 16, 1024);
-          mma_f16(d, ad, bd, IDESC, (seg_start && ks == 0) ? 0u : 1u);
+        for (int j = 0; j < SK_TPU; ++j) {
+          const uint32_t sWj = sW + j * (SK_BN * 128);
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks) {
+            const uint64_t ad = W_MN ? make_sw128_desc(sWj + ks * 2048, 64 * 128, 1024)
+                                     : make_sw128_desc(sWj + ks * 32, 16, 1024);
+            mma_f16(d + j * SK_MN, ad, bd0 + static_cast<uint64_t>((ks * 32) >> 4), IDESC,
+                    (seg_start && ks == 0) ? 0u : 1u);
+          }
         }
         mma_commit(empty_bar(stage));
         if (++stage == SK_STAGES) {
           stage = 0;
           phase ^= 1u;
         }
+        seg_start = false;
         if (seg_end) {
           mma_commit(tfull_bar(acc));
-          seg_open = false;
-          acc ^= 1;
-          if (acc == 0) acc_phase ^= 1u;
+          seg_start = true;
+          if (++acc == SK_NBUF) {
+            acc = 0;
+            acc_phase ^= 1u;
+          }
         }
+        if (++kb == p.KB) kb = 0;
       }
-      (void)seg_open;
       mma_commit(done_bar);
       mbar_wait_drain(done_bar, 0, p.budget);
     }
     __syncwarp();
   } else {
-    // epilogue: 128 threads, thread <-> one column n of the tile, 16 values (rows m)
+    // ── epilogue: 128 threads, thread <-> one column of each tile of the group
     const int q = warp & 3;
     const int etid = threadIdx.x - 64;  // 0..127
     int acc = 0;
     uint32_t acc_phase = 0;
-    long long u = ub;
-    while (u < ue) {
-      const int t = static_cast<int>(u / p.KB);
-      const long long seg_last = min(ue, static_cast<long long>(t + 1) * p.KB);
-      u = seg_last;
+    int g = g_begin, kb = kb_begin, left = n_units;
+    while (left > 0) {
+      const int seg_units = min(left, p.KB - kb);
+      const bool whole_from_start = (kb == 0);
+      left -= seg_units;
+      // A row bias is loaded before the accumulator is ready, off the tail.
+      float bias_pre[SK_TPU];
+#pragma unroll
+      for (int j = 0; j < SK_TPU; ++j) {
+        const int n = (g * SK_TPU + j) * SK_BN + q * 32 + lane;
+        bias_pre[j] = (ep.operand_kind == OJX_OPERAND_ROW && n < p.N)
+                          ? load_elem(ep.operand, n, ep.dtype_operand)
+                          : 0.0f;
+      }
       // The four epilogue warps meet at named barriers below, so they must agree
       // on whether to go on: any warp that failed its wait stops all four.
       const bool waited = mbar_wait(tfull_bar(acc), acc_phase, p.budget, s_abort);
       if (named_bar_red_or(1, 128, !waited)) break;
       tc_fence_after();
-      uint32_t r[16];
-      tmem_ld16(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * SK_MN),
-                r);
+      uint32_t r[SK_TPU][16];
+      const uint32_t tq = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                          static_cast<uint32_t>(acc * SK_TPU * SK_MN);
+#pragma unroll
+      for (int j = 0; j < SK_TPU; ++j) tmem_ld16(tq + j * SK_MN, r[j]);
       tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty_bar(acc));
-      acc ^= 1;
-      if (acc == 0) acc_phase ^= 1u;
+      if (++acc == SK_NBUF) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+      float v[SK_TPU][SK_MN];
+#pragma unroll
+      for (int j = 0; j < SK_TPU; ++j)
+#pragma unroll
+        for (int m = 0; m < SK_MN; ++m) v[j][m] = __uint_as_float(r[j][m]);
 
-      float v[SK_MN];
-#pragma unroll
-      for (int m = 0; m < SK_MN; ++m) v[m] = __uint_as_float(r[m]);
-      const int c_first = cta_of_unit(static_cast<long long>(t) * p.KB, p);
-      const int c_last = cta_of_unit(min(static_cast<long long>(t + 1) * p.KB, p.U) - 1, p);
-      const int ncontrib = c_last - c_first + 1;
-      const int n = t * SK_BN + q * 32 + lane;
       bool finish = true;
-      if (ncontrib > 1) {
-        const int j = blockIdx.x - c_first;
-        float* slot = p.partials + (static_cast<long long>(t) * p.maxc + j) * (SK_MN * SK_BN);
+      const bool whole = whole_from_start && seg_units == p.KB;
+      if (!whole) {
+        const int c_first = cta_of_unit(static_cast<long long>(g) * p.KB, p);
+        const int c_last = cta_of_unit(min(static_cast<long long>(g + 1) * p.KB, p.U) - 1, p);
+        const int ncontrib = c_last - c_first + 1;
+        const int jc = blockIdx.x - c_first;
+        float* slot = p.partials + (static_cast<long long>(g) * p.maxc + jc) * SK_SLOT +
+                      q * 32 + lane;
 #pragma unroll
-        for (int m = 0; m < SK_MN; ++m)
-          if (m < p.M) slot[m * SK_BN + q * 32 + lane] = v[m];
+        for (int j = 0; j < SK_TPU; ++j)
+#pragma unroll
+          for (int m = 0; m < SK_MN; ++m)
+            if (m < p.M) slot[(j * SK_MN + m) * SK_BN] = v[j][m];
         named_bar_sync(1, 128);
         if (etid == 0) {
           __threadfence();
-          unsigned long long* ctr = p.counters + t;
+          unsigned long long* ctr = p.counters + g;
           unsigned long long old = *reinterpret_cast<volatile unsigned long long*>(ctr);
-          unsigned long long seen;
           unsigned int count;
-          while (true) {  // bounded: ends as soon as the CAS succeeds
+          while (true) {  // ends as soon as the CAS succeeds
             const unsigned int e = static_cast<unsigned int>(old >> 32);
             count = (e == p.epoch) ? static_cast<unsigned int>(old & 0xffffffffu) + 1u : 1u;
             const unsigned long long nv = (static_cast<unsigned long long>(p.epoch) << 32) | count;
-            seen = atomicCAS(ctr, old, nv);
+            const unsigned long long seen = atomicCAS(ctr, old, nv);
             if (seen == old) break;
             old = seen;
           }
@@ -245,25 +288,60 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
         named_bar_sync(1, 128);
         finish = *s_last != 0;
         if (finish) {
-          const float* base = p.partials + static_cast<long long>(t) * p.maxc * (SK_MN * SK_BN);
+          // Sum the partials in contributor order; every load is issued before
+          // the first add of a contributor's slot.
+          const float* base = p.partials + static_cast<long long>(g) * p.maxc * SK_SLOT + q * 32 + lane;
 #pragma unroll
-          for (int m = 0; m < SK_MN; ++m) v[m] = 0.0f;
+          for (int j = 0; j < SK_TPU; ++j)
+#pragma unroll
+            for (int m = 0; m < SK_MN; ++m) v[j][m] = 0.0f;
           for (int jj = 0; jj < ncontrib; ++jj) {
-            const float* sl = base + static_cast<long long>(jj) * (SK_MN * SK_BN);
+            const float* sl = base + static_cast<long long>(jj) * SK_SLOT;
+            float t[SK_TPU][SK_MN];
 #pragma unroll
-            for (int m = 0; m < SK_MN; ++m)
-              if (m < p.M) v[m] += __ldcg(sl + m * SK_BN + q * 32 + lane);
+            for (int j = 0; j < SK_TPU; ++j)
+#pragma unroll
+              for (int m = 0; m < SK_MN; ++m)
+                t[j][m] = m < p.M ? __ldcg(sl + (j * SK_MN + m) * SK_BN) : 0.0f;
+#pragma unroll
+            for (int j = 0; j < SK_TPU; ++j)
+#pragma unroll
+              for (int m = 0; m < SK_MN; ++m) v[j][m] += t[j][m];
           }
         }
         named_bar_sync(1, 128);  // s_last may be rewritten by the next segment
       }
-      if (finish && n < p.N) {
+      if (finish) {
 #pragma unroll
-        for (int m = 0; m < SK_MN; ++m)
-          if (m < p.M)
-            store_elem(ep.c, static_cast<int64_t>(m) * ep.ldc + n, ep.dtype_c,
-                       epilogue_value(ep, v[m], m, n));
+        for (int j = 0; j < SK_TPU; ++j) {
+          const int n = (g * SK_TPU + j) * SK_BN + q * 32 + lane;
+          if (n < p.N) {
+            // All operand loads first, then the op chain 16-wide, then the stores:
+            // interleaving them would serialise every load behind the previous
+            // store (C may alias the operand as far as the compiler knows).
+            if (ep.operand_kind != OJX_OPERAND_NONE) {
+              float x[SK_MN];
+              if (ep.operand_kind == OJX_OPERAND_ROW) {
+#pragma unroll
+                for (int m = 0; m < SK_MN; ++m) x[m] = bias_pre[j];
+              } else {
+#pragma unroll
+                for (int m = 0; m < SK_MN; ++m)
+                  x[m] = m < p.M ? load_elem(ep.operand, static_cast<int64_t>(m) * ep.ld_operand + n,
+                                             ep.dtype_operand)
+                                 : 0.0f;
+              }
+              binary16(ep.binary_op, ep.operand_is_lhs != 0, v[j], x);
+            }
+            for (int i = 0; i < ep.n_unary; ++i) unary16(unary_at(ep.unary_packed, i), v[j]);
+#pragma unroll
+            for (int m = 0; m < SK_MN; ++m)
+              if (m < p.M) store_elem(ep.c, static_cast<int64_t>(m) * ep.ldc + n, ep.dtype_c, v[j][m]);
+          }
+        }
       }
+      kb = 0;
+      ++g;
     }
   }
 
@@ -271,7 +349,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, 32);
+    tmem_dealloc(tmem_base, SK_TMEM_COLS);
   }
 }
 
@@ -287,7 +365,7 @@ bool skinny_supported(const ojx_gemm_desc& d) {
 static std::atomic<unsigned int> g_skinny_epoch{1};
 
 // Host-side partition bookkeeping; mirrors unit_begin / cta_of_unit.
-static int skinny_max_contrib(int n_tiles, int KB, long long U, int G) {
+static int skinny_max_contrib(int n_groups, int KB, long long U, int G) {
   auto ub = [&](long long c) { return c * U / G; };
   auto cta_of = [&](long long u) {
     long long c = (u * G) / U;
@@ -296,9 +374,9 @@ static int skinny_max_contrib(int n_tiles, int KB, long long U, int G) {
     return c;
   };
   int mx = 1;
-  for (int t = 0; t < n_tiles; ++t) {
-    const long long a = cta_of(static_cast<long long>(t) * KB);
-    const long long b = cta_of(std::min<long long>(static_cast<long long>(t + 1) * KB, U) - 1);
+  for (int g = 0; g < n_groups; ++g) {
+    const long long a = cta_of(static_cast<long long>(g) * KB);
+    const long long b = cta_of(std::min<long long>(static_cast<long long>(g + 1) * KB, U) - 1);
     mx = std::max<int>(mx, static_cast<int>(b - a + 1));
   }
   return mx;
@@ -309,17 +387,17 @@ int launch_skinny_gemm(const ojx_gemm_desc& d, cudaStream_t s) {
   p.M = static_cast<int>(d.M);
   p.N = static_cast<int>(d.N);
   p.K = static_cast<int>(d.K);
-  p.n_tiles = (p.N + SK_BN - 1) / SK_BN;
+  p.n_groups = (p.N + SK_TPU * SK_BN - 1) / (SK_TPU * SK_BN);
   p.KB = (p.K + SK_BK - 1) / SK_BK;
-  p.U = static_cast<long long>(p.n_tiles) * p.KB;
+  p.U = static_cast<long long>(p.n_groups) * p.KB;
   const DeviceProps& dp = current_props();
   p.G = static_cast<int>(std::min<long long>(p.U, dp.sm_count));
-  p.maxc = skinny_max_contrib(p.n_tiles, p.KB, p.U, p.G);
-  const size_t part_bytes = static_cast<size_t>(p.n_tiles) * p.maxc * SK_MN * SK_BN * 4;
+  p.maxc = skinny_max_contrib(p.n_groups, p.KB, p.U, p.G);
+  const size_t part_bytes = static_cast<size_t>(p.n_groups) * p.maxc * SK_SLOT * 4;
   p.partials = static_cast<float*>(stream_workspace(s, part_bytes, 1, false));
   if (!p.partials) return OJX_ERR_OOM;
   p.counters = static_cast<unsigned long long*>(
-      stream_workspace(s, static_cast<size_t>(p.n_tiles) * 8, 2, /*zero=*/true));
+      stream_workspace(s, static_cast<size_t>(p.n_groups) * 8, 2, /*zero=*/true));
   if (!p.counters) return OJX_ERR_OOM;
   p.epoch = g_skinny_epoch.fetch_add(1);
   if (p.epoch == 0) p.epoch = g_skinny_epoch.fetch_add(1);
@@ -340,9 +418,7 @@ int launch_skinny_gemm(const ojx_gemm_desc& d, cudaStream_t s) {
   const EpiParams ep = make_epi(d);
   const bool bf = d.dtype_a == OJX_BF16;
   auto launch = [&](auto kern) {
-    int r = cuda_status(
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SK_SMEM),
-        "cudaFuncSetAttribute(skinny)");
+    int r = ensure_smem_attr(reinterpret_cast<const void*>(kern), SK_SMEM);
     if (r) return r;
     kern<<<p.G, SK_THREADS, SK_SMEM, s>>>(tw, tx, ep, p);
     g_launches.fetch_add(1);

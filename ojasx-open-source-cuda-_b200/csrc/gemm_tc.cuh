@@ -385,9 +385,7 @@ static int run_tc(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap&
                   cudaStream_t s) {
   using L = TcLayout<KIND, BN, STAGES>;
   auto kern = tc_gemm_kernel<KIND, FMT, A_MN, B_MN, BN, STAGES>;
-  int st = cuda_status(
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM_BYTES),
-      "cudaFuncSetAttribute(tc_gemm)");
+  int st = ensure_smem_attr(reinterpret_cast<const void*>(kern), L::SMEM_BYTES);
   if (st) return st;
   const DeviceProps& p = current_props();
   const long tiles = static_cast<long>((M + TC_BM - 1) / TC_BM) * ((N + BN - 1) / BN);

@@ -34,6 +34,9 @@ const DeviceProps& current_props();
 // nullptr and sets the error on failure.
 void* stream_workspace(cudaStream_t s, size_t bytes, int slot, bool zero);
 
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (kernel, device).
+int ensure_smem_attr(const void* kernel, int bytes);
+
 // Kernel families (implemented in the .cu files).
 int launch_tc_gemm(const ojx_gemm_desc& d, cudaStream_t s);
 int launch_tc_gemm_3xtf32(const ojx_gemm_desc& d, cudaStream_t s);

@@ -44,6 +44,21 @@ int cuda_status(cudaError_t e, const char* what) {
 
 void set_last_route(int route) { t_last_route = route; }
 
+int ensure_smem_attr(const void* kernel, int bytes) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, int>* done = new std::map<std::pair<const void*, int>, int>();
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> g(mu);
+  auto key = std::make_pair(kernel, dev);
+  auto it = done->find(key);
+  if (it != done->end() && it->second >= bytes) return OJX_OK;
+  int st = cuda_status(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes),
+                       "cudaFuncSetAttribute");
+  if (!st) (*done)[key] = bytes;
+  return st;
+}
+
 const DeviceProps& current_props() {
   static std::mutex mu;
   static DeviceProps props[128];
