@@ -183,7 +183,10 @@ def _metric(cfg) -> str:
 def _config_block(args, cfg, world) -> dict:
     return {"workload": f"{args.config}: {cfg['desc']}", "M": cfg["M"], "N": cfg["N"], "K": cfg["K"],
             "epilogue": f"{cfg['act']}(acc + bias[N])",
-            "parallelism": f"N-shard{world}" if world > 1 else "single GPU",
+            "parallelism": (f"N-shard{world}, C gathered by the GEMM epilogue over NVLink"
+                            if getattr(args, "gather", "p2p") == "p2p" else
+                            f"N-shard{world}, C gathered by NCCL all_gather + re-layout")
+                           if world > 1 else "single GPU",
             "l2": "inputs larger than L2" if cfg["K"] * cfg["N"] * (2 if cfg["dtype"] == "bf16" else 4) > L2_BYTES
                   else "L2 flushed (256 MiB write) between timed iterations"}
 
@@ -222,29 +225,36 @@ def run_ours(args, cfg, world, rank, local):
             del blk
     bias_full = (torch.randn(N, device=dev, generator=g) * cfg["b_scale"]).to(tdt)
     bias = bias_full[rank * Nl:(rank + 1) * Nl].contiguous()
-    C_local = torch.empty(M, Nl, device=dev, dtype=tdt)
-    C = torch.empty(M, N, device=dev, dtype=tdt) if world > 1 else C_local
-    gathered = torch.empty(world * M * Nl, device=dev, dtype=tdt) if world > 1 else None
     flush = torch.empty(256 * 1024 * 1024, device=dev, dtype=torch.uint8)
     needs_flush = K * Nl * es < L2_BYTES
     stream = torch.cuda.current_stream(dev)
     sp = stream.cuda_stream
+    sharded = None
+    if world > 1:
+        from torchcl.mesh import ShardedGemm
+        sharded = ShardedGemm(M, N, K, dtype="bf16" if code == L.BF16 else "fp16",
+                              strategy=args.gather, stream=sp)
+        C = sharded.c_view()
+    else:
+        C = torch.empty(M, N, device=dev, dtype=tdt)
 
     d = L.GemmDesc()
     d.M, d.N, d.K = M, Nl, K
     d.dtype_a = d.dtype_b = d.dtype_c = d.dtype_operand = code
-    d.a, d.b, d.c, d.operand = A.data_ptr(), W.data_ptr(), C_local.data_ptr(), bias.data_ptr()
+    d.a, d.b, d.c, d.operand = A.data_ptr(), W.data_ptr(), C.data_ptr(), bias.data_ptr()
     d.operand_kind, d.binary_op = L.OPERAND_ROW, L.BINARY["add"]
     d.n_unary, d.unary[0] = 1, L.UNARY[cfg["act"]]
     d.fp32_mode = L.FP32_3XTF32 if code == L.F32 and M > 16 else L.FP32_AUTO
 
     def gemm():
-        L.check(lib.ojx_gemm(ctypes.byref(d), sp), "ojx_gemm")
+        if sharded is not None:
+            sharded.launch(A.data_ptr(), W.data_ptr(), bias.data_ptr(), (cfg["act"],))
+        else:
+            L.check(lib.ojx_gemm(ctypes.byref(d), sp), "ojx_gemm")
 
     def gather():
-        if world > 1:
-            dist.all_gather_into_tensor(gathered, C_local.view(-1))
-            C.view(M, world, Nl).copy_(gathered.view(world, M, Nl).transpose(0, 1))
+        if sharded is not None:
+            sharded.barrier()
 
     # warm-up
     for _ in range(args.warmup):
@@ -322,6 +332,8 @@ def run_ours(args, cfg, world, rank, local):
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
+        torch.cuda.synchronize(dev)
+        sharded.close()
         dist.destroy_process_group()
     return 0
 
@@ -389,6 +401,8 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--config", default="cfg5", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--gather", default="p2p", choices=["p2p", "nccl"],
+                    help="multi-GPU: all-gather fused into the GEMM epilogue (p2p) or NCCL")
     ap.add_argument("--m", type=int, default=None, help="override M (e.g. cfg4 M in {1,4,16})")
     ap.add_argument("--size", type=int, default=None, help="override M=N=K (cfg2 sweep)")
     args = ap.parse_args()

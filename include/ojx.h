@@ -76,6 +76,8 @@ enum {
 };
 
 #define OJX_MAX_UNARY 8
+#define OJX_MAX_PEERS 8        /* ranks an all-gathering GEMM can write to */
+#define OJX_IPC_HANDLE_BYTES 64
 
 /* One GEMM with its fused epilogue:
  *   acc[m,n] = sum_k op(A)[m,k] * op(B)[k,n]              (fp32 accumulate)
@@ -211,6 +213,27 @@ int ojx_fill(void* out, double value, int64_t n, int32_t dtype, ojx_stream s);
 /* dtype conversion.  Replaces AdaptivePrecision pack/unpack (torchcl/liquid/precision.py:68-103,
  * precision.cl:7-27). */
 int ojx_cast(void* out, int32_t dtype_out, const void* in, int32_t dtype_in, int64_t n, ojx_stream s);
+
+/* ── multi-GPU: W column-sharded GEMM with the output all-gathered by the GEMM
+ * epilogue itself.  The reference's only "distributed" code is a host-side loop
+ * (torchcl/mesh/collective.py:33-91: to_cpu, torch.cat, to_opencl); there is no
+ * device-side counterpart, so these entry points are new.
+ *
+ * Each rank allocates its full C[M, N_total] (ojx_malloc), exports it with
+ * ojx_ipc_get_handle, exchanges the 64-byte handles out of band (e.g. a
+ * torch.distributed all_gather_object) and opens the peers' buffers with
+ * ojx_ipc_open_handle.  ojx_gemm_allgather then computes this rank's column
+ * block C[:, col_offset : col_offset + d->N] = epilogue(A @ W_shard) and stores
+ * every output chunk into ALL ranks' C buffers (c_peers[i], row-major, leading
+ * dimension d->ldc) over NVLink, so no separate all-gather or re-layout runs.
+ * The kernel makes its stores visible system-wide before it completes; a
+ * stream-ordered barrier across the ranks (one small collective) must follow
+ * before any rank reads its C. */
+int ojx_ipc_get_handle(void* dptr, void* handle_out);               /* 64 bytes */
+int ojx_ipc_open_handle(const void* handle, void** dptr);           /* peer's buffer */
+int ojx_ipc_close_handle(void* dptr);
+int ojx_gemm_allgather(const ojx_gemm_desc* d, void* const* c_peers, int32_t n_peers,
+                       int64_t col_offset, ojx_stream s);
 
 /* Test hook: the next ojx_gemm on a tcgen05 route runs with its TMA producer
  * silenced, so the MMA warp's bounded wait must expire and the kernel must

@@ -82,10 +82,18 @@ struct EpiParams {
   int32_t operand_is_lhs;
   int32_t n_unary;
   uint32_t unary_packed;
+  // Output destinations: dst[0..n_dst) all receive the same values at
+  // (row * ldc + col_offset + col).  One destination (c, offset 0) for a plain
+  // GEMM; every rank's C buffer for an all-gathering sharded GEMM.
+  int32_t n_dst;
+  int64_t col_offset;
+  void* dst[OJX_MAX_PEERS];
 };
 
-// Host: copy the epilogue fields of a GEMM descriptor.
-EpiParams make_epi(const ojx_gemm_desc& d);
+struct Dests;
+// Host: copy the epilogue fields of a GEMM descriptor (and the destinations of an
+// all-gathering GEMM, when given).
+EpiParams make_epi(const ojx_gemm_desc& d, const Dests* dests = nullptr);
 
 __device__ __forceinline__ int unary_at(uint32_t packed, int i) {
   return static_cast<int>((packed >> (4 * i)) & 15u);

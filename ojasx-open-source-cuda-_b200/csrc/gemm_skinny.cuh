@@ -335,14 +335,21 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
             }
             for (int i = 0; i < ep.n_unary; ++i) unary16(unary_at(ep.unary_packed, i), v[j]);
 #pragma unroll
-            for (int m = 0; m < SK_MN; ++m)
-              if (m < p.M) store_elem(ep.c, static_cast<int64_t>(m) * ep.ldc + n, ep.dtype_c, v[j][m]);
+            for (int di = 0; di < OJX_MAX_PEERS; ++di) {
+              if (di >= ep.n_dst) break;
+#pragma unroll
+              for (int m = 0; m < SK_MN; ++m)
+                if (m < p.M)
+                  store_elem(ep.dst[di], static_cast<int64_t>(m) * ep.ldc + ep.col_offset + n,
+                             ep.dtype_c, v[j][m]);
+            }
           }
         }
       }
       kb = 0;
       ++g;
     }
+    if (ep.n_dst > 1) __threadfence_system();  // peer stores visible before completion
   }
 
   tc_fence_before();
@@ -382,7 +389,7 @@ static int skinny_max_contrib(int n_groups, int KB, long long U, int G) {
   return mx;
 }
 
-int launch_skinny_gemm(const ojx_gemm_desc& d, cudaStream_t s) {
+int launch_skinny_gemm(const ojx_gemm_desc& d, cudaStream_t s, const Dests* dests) {
   SkinnyParams p{};
   p.M = static_cast<int>(d.M);
   p.N = static_cast<int>(d.N);
@@ -415,7 +422,7 @@ int launch_skinny_gemm(const ojx_gemm_desc& d, cudaStream_t s) {
     st = make_tmap_2d_sw128(&tw, tdt, 2, d.b, p.K, p.N, d.ldb * 2, 64, SK_BN);
   if (st) return st;
   if ((st = make_tmap_2d_sw128(&tx, tdt, 2, d.a, p.K, p.M, d.lda * 2, 64, SK_MN))) return st;
-  const EpiParams ep = make_epi(d);
+  const EpiParams ep = make_epi(d, dests);
   const bool bf = d.dtype_a == OJX_BF16;
   auto launch = [&](auto kern) {
     int r = ensure_smem_attr(reinterpret_cast<const void*>(kern), SK_SMEM);

@@ -92,32 +92,41 @@ __device__ __forceinline__ void store_row16(const EpiParams& ep, const uint32_t 
   for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
   epilogue16(ep, v, row, col0, valid);
   const int esz = ep.dtype_c == OJX_F32 ? 4 : 2;
-  char* dst = static_cast<char*>(ep.c) + (row * ep.ldc + col0) * esz;
-  if (valid == 16 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
-    if (ep.dtype_c == OJX_F32) {
-      float4* d4 = reinterpret_cast<float4*>(dst);
+  const int64_t off = (row * ep.ldc + ep.col_offset + col0) * esz;
+  uint32_t p[8];
+  if (ep.dtype_c != OJX_F32) {
 #pragma unroll
-      for (int j = 0; j < 4; ++j) d4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-    } else {
-      uint32_t p[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        if (ep.dtype_c == OJX_BF16) {
-          __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
-          p[j] = *reinterpret_cast<uint32_t*>(&h);
-        } else {
-          __half2 h = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
-          p[j] = *reinterpret_cast<uint32_t*>(&h);
-        }
+    for (int j = 0; j < 8; ++j) {
+      if (ep.dtype_c == OJX_BF16) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+        p[j] = *reinterpret_cast<uint32_t*>(&h);
+      } else {
+        __half2 h = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+        p[j] = *reinterpret_cast<uint32_t*>(&h);
       }
-      uint4* d4 = reinterpret_cast<uint4*>(dst);
-      d4[0] = make_uint4(p[0], p[1], p[2], p[3]);
-      d4[1] = make_uint4(p[4], p[5], p[6], p[7]);
     }
-  } else {
+  }
+  // Static loop over the destination slots (no dynamic indexing of the
+  // parameter array); slot i is used when i < n_dst.
 #pragma unroll
-    for (int j = 0; j < 16; ++j)
-      if (j < valid) store_elem(ep.c, row * ep.ldc + col0 + j, ep.dtype_c, v[j]);
+  for (int di = 0; di < OJX_MAX_PEERS; ++di) {
+    if (di >= ep.n_dst) break;
+    char* dst = static_cast<char*>(ep.dst[di]) + off;
+    if (valid == 16 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+      if (ep.dtype_c == OJX_F32) {
+        float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) d4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+      } else {
+        uint4* d4 = reinterpret_cast<uint4*>(dst);
+        d4[0] = make_uint4(p[0], p[1], p[2], p[3]);
+        d4[1] = make_uint4(p[4], p[5], p[6], p[7]);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        if (j < valid) store_elem(ep.dst[di], row * ep.ldc + ep.col_offset + col0 + j, ep.dtype_c, v[j]);
+    }
   }
 }
 
@@ -303,6 +312,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
+    // Stores into other GPUs' memory become visible system-wide before the
+    // kernel completes (the cross-rank barrier that follows relies on it).
+    if (ep.n_dst > 1) __threadfence_system();
   }
 
   tc_fence_before();
@@ -361,7 +373,7 @@ __global__ void __launch_bounds__(256) split_tf32_kernel(const float* __restrict
 
 // ── host side ────────────────────────────────────────────────────────────────
 
-EpiParams make_epi(const ojx_gemm_desc& d) {
+EpiParams make_epi(const ojx_gemm_desc& d, const Dests* dests) {
   EpiParams ep{};
   ep.c = d.c;
   ep.ldc = d.ldc;
@@ -376,6 +388,14 @@ EpiParams make_epi(const ojx_gemm_desc& d) {
   ep.unary_packed = 0;
   for (int i = 0; i < d.n_unary && i < OJX_MAX_UNARY; ++i)
     ep.unary_packed |= (static_cast<uint32_t>(d.unary[i]) & 15u) << (4 * i);
+  ep.n_dst = 1;
+  ep.col_offset = 0;
+  for (int i = 0; i < OJX_MAX_PEERS; ++i) ep.dst[i] = d.c;
+  if (dests) {
+    ep.n_dst = dests->n;
+    ep.col_offset = dests->col_offset;
+    for (int i = 0; i < dests->n && i < OJX_MAX_PEERS; ++i) ep.dst[i] = dests->p[i];
+  }
   return ep;
 }
 
@@ -405,7 +425,7 @@ bool tc_gemm_supported(const ojx_gemm_desc& d) {
   return true;
 }
 
-int launch_tc_gemm(const ojx_gemm_desc& d, cudaStream_t s) {
+int launch_tc_gemm(const ojx_gemm_desc& d, cudaStream_t s, const Dests* dests) {
   const int M = static_cast<int>(d.M), N = static_cast<int>(d.N), K = static_cast<int>(d.K);
   const CUtensorMapDataType tdt =
       d.dtype_a == OJX_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -427,7 +447,7 @@ int launch_tc_gemm(const ojx_gemm_desc& d, cudaStream_t s) {
   else
     st = make_tmap_2d_sw128(&tb, tdt, 2, d.b, K, N, d.ldb * 2, 64, BN);
   if (st) return st;
-  const EpiParams ep = make_epi(d);
+  const EpiParams ep = make_epi(d, dests);
   const bool bf = d.dtype_a == OJX_BF16;
   const int am = d.trans_a ? 1 : 0, bm = d.trans_b ? 0 : 1;
 #define OJX_TC_CASE(FMTV, AMN, BMN, BNV)                                                  \

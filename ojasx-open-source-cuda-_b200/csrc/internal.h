@@ -37,10 +37,18 @@ void* stream_workspace(cudaStream_t s, size_t bytes, int slot, bool zero);
 // cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (kernel, device).
 int ensure_smem_attr(const void* kernel, int bytes);
 
-// Kernel families (implemented in the .cu files).
-int launch_tc_gemm(const ojx_gemm_desc& d, cudaStream_t s);
+// Output destinations of an all-gathering GEMM (every rank's C buffer).
+struct Dests {
+  int n;
+  int64_t col_offset;
+  void* p[OJX_MAX_PEERS];
+};
+
+// Kernel families (implemented in the .cu files).  `dests` (optional) replaces
+// the single output d.c by several buffers written with the same values.
+int launch_tc_gemm(const ojx_gemm_desc& d, cudaStream_t s, const Dests* dests = nullptr);
 int launch_tc_gemm_3xtf32(const ojx_gemm_desc& d, cudaStream_t s);
-int launch_skinny_gemm(const ojx_gemm_desc& d, cudaStream_t s);
+int launch_skinny_gemm(const ojx_gemm_desc& d, cudaStream_t s, const Dests* dests = nullptr);
 int launch_simt_gemm(const ojx_gemm_desc& d, cudaStream_t s);
 bool tc_gemm_supported(const ojx_gemm_desc& d);
 bool skinny_supported(const ojx_gemm_desc& d);

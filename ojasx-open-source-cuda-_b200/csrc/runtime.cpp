@@ -566,6 +566,73 @@ int ojx_cast(void* out, int32_t dtype_out, const void* in, int32_t dtype_in, int
   return launch_cast(out, dtype_out, in, dtype_in, n, static_cast<cudaStream_t>(s));
 }
 
+int ojx_ipc_get_handle(void* dptr, void* handle_out) {
+  if (!dptr || !handle_out) return set_error(OJX_ERR_INVALID, "ojx_ipc_get_handle: NULL pointer");
+  static_assert(sizeof(cudaIpcMemHandle_t) == OJX_IPC_HANDLE_BYTES, "IPC handle size");
+  cudaIpcMemHandle_t h;
+  int st = cuda_status(cudaIpcGetMemHandle(&h, dptr), "cudaIpcGetMemHandle");
+  if (!st) std::memcpy(handle_out, &h, sizeof(h));
+  return st;
+}
+
+int ojx_ipc_open_handle(const void* handle, void** dptr) {
+  if (!handle || !dptr) return set_error(OJX_ERR_INVALID, "ojx_ipc_open_handle: NULL pointer");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  return cuda_status(cudaIpcOpenMemHandle(dptr, h, cudaIpcMemLazyEnablePeerAccess),
+                     "cudaIpcOpenMemHandle");
+}
+
+int ojx_ipc_close_handle(void* dptr) {
+  return cuda_status(cudaIpcCloseMemHandle(dptr), "cudaIpcCloseMemHandle");
+}
+
+int ojx_gemm_allgather(const ojx_gemm_desc* in, void* const* c_peers, int32_t n_peers,
+                       int64_t col_offset, ojx_stream stream) {
+  set_last_route(OJX_ROUTE_NONE);
+  if (!in || !c_peers) return set_error(OJX_ERR_INVALID, "ojx_gemm_allgather: NULL argument");
+  if (n_peers < 1 || n_peers > OJX_MAX_PEERS)
+    return set_error(OJX_ERR_INVALID, "ojx_gemm_allgather: %d peers (1..%d)", n_peers, OJX_MAX_PEERS);
+  if (col_offset < 0) return set_error(OJX_ERR_INVALID, "ojx_gemm_allgather: negative column offset");
+  ojx_gemm_desc d = *in;
+  for (int i = 0; i < n_peers; ++i)
+    if (!c_peers[i]) return set_error(OJX_ERR_INVALID, "ojx_gemm_allgather: peer %d is NULL", i);
+  if (d.M <= 0 || d.N <= 0 || d.K <= 0)
+    return set_error(OJX_ERR_INVALID, "ojx_gemm_allgather: empty problem");
+  if (d.ldc == 0) return set_error(OJX_ERR_INVALID, "ojx_gemm_allgather: ldc (the full row length) is required");
+  if (d.ldc < col_offset + d.N)
+    return set_error(OJX_ERR_INVALID, "ojx_gemm_allgather: column block exceeds ldc");
+  if (d.lda == 0) d.lda = d.trans_a ? d.M : d.K;
+  if (d.ldb == 0) d.ldb = d.trans_b ? d.K : d.N;
+  if (d.ld_operand == 0) d.ld_operand = d.N;
+  if (d.n_unary < 0 || d.n_unary > OJX_MAX_UNARY) return set_error(OJX_ERR_INVALID, "bad n_unary");
+  for (int i = 0; i < d.n_unary; ++i)
+    if (!valid_unary(d.unary[i])) return set_error(OJX_ERR_INVALID, "unknown unary op %d", d.unary[i]);
+  if (d.operand_kind != OJX_OPERAND_NONE &&
+      (!d.operand || !valid_binary(d.binary_op) || !valid_dtype(d.dtype_operand)))
+    return set_error(OJX_ERR_INVALID, "ojx_gemm_allgather: bad epilogue operand");
+  if (current_props().cc_major < 10)
+    return set_error(OJX_ERR_NOT_INITIALIZED, "ojx_gemm_allgather: current device is not sm_100");
+  d.c = c_peers[0];
+  Dests dests{};
+  dests.n = n_peers;
+  dests.col_offset = col_offset;
+  for (int i = 0; i < n_peers; ++i) dests.p[i] = c_peers[i];
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int st;
+  if (!(d.flags & OJX_GEMM_FLAG_NO_SKINNY) && d.M <= 16 && skinny_supported(d)) {
+    st = launch_skinny_gemm(d, s, &dests);
+    if (!st) set_last_route(OJX_ROUTE_SKINNY);
+  } else if (tc_gemm_supported(d)) {
+    st = launch_tc_gemm(d, s, &dests);
+    if (!st) set_last_route(OJX_ROUTE_TC_F16);
+  } else {
+    st = set_error(OJX_ERR_UNSUPPORTED,
+                   "ojx_gemm_allgather: needs bf16/fp16 operands with 16-byte aligned rows");
+  }
+  return st;
+}
+
 int ojx_debug_silence_producer_once(void) {
   g_silence_producer_once.store(1);
   return OJX_OK;

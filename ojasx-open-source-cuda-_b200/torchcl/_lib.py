@@ -30,6 +30,8 @@ FP32_AUTO, FP32_3XTF32, FP32_FFMA = 0, 1, 2
 FLAG_FORCE_SIMT, FLAG_NO_SKINNY, FLAG_FORCE_SKINNY = 0x1, 0x2, 0x4
 ROUTES = {0: "none", 1: "tc_f16", 2: "tc_3xtf32", 3: "skinny", 4: "simt"}
 MAX_UNARY = 8
+MAX_PEERS = 8
+IPC_HANDLE_BYTES = 64
 
 
 class TimeoutError_(RuntimeError):
@@ -110,6 +112,11 @@ _SIGS = {
     "ojx_transpose": ([_P, _P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int32, _P], ctypes.c_int),
     "ojx_fill": ([_P, ctypes.c_double, ctypes.c_int64, ctypes.c_int32, _P], ctypes.c_int),
     "ojx_cast": ([_P, ctypes.c_int32, _P, ctypes.c_int32, ctypes.c_int64, _P], ctypes.c_int),
+    "ojx_ipc_get_handle": ([_P, _P], ctypes.c_int),
+    "ojx_ipc_open_handle": ([_P, ctypes.POINTER(_P)], ctypes.c_int),
+    "ojx_ipc_close_handle": ([_P], ctypes.c_int),
+    "ojx_gemm_allgather": ([ctypes.POINTER(GemmDesc), ctypes.POINTER(_P), ctypes.c_int32,
+                            ctypes.c_int64, _P], ctypes.c_int),
     "ojx_debug_silence_producer_once": ([], ctypes.c_int),
 }
 
