@@ -235,6 +235,18 @@ int ojx_ipc_close_handle(void* dptr);
 int ojx_gemm_allgather(const ojx_gemm_desc* d, void* const* c_peers, int32_t n_peers,
                        int64_t col_offset, ojx_stream s);
 
+/* Decode GEMM (the skinny split-K route of ojx_gemm: 1 <= M <= 16, bf16 or fp16
+ * A and B, A row-major, 16-byte aligned rows) that allocates no device memory.
+ * No counterpart in the reference.  For callers that may not have the library
+ * call cudaMalloc: engines that reserve the GPU's memory up front and treat
+ * later allocations as failures, or latency-critical loops in which an
+ * allocation could synchronise the device.  Its scratch is a fixed 8 MiB array
+ * that every GPU loading the library holds until exit; larger problems are
+ * rejected with OJX_ERR_INVALID.  All calls share the array: calls that overlap
+ * on the GPU race, so order them on one stream.  The first call on a device sets
+ * the array up; make it before capturing a stream. */
+int ojx_gemm_skinny_noalloc(const ojx_gemm_desc* d, ojx_stream s);
+
 /* Test hook: the next ojx_gemm on a tcgen05 route runs with its TMA producer
  * silenced, so the MMA warp's bounded wait must expire and the kernel must
  * return with OJX_ERR_TIMEOUT recorded (read it with ojx_poll_device_error). */

@@ -16,4 +16,10 @@ int make_tmap_2d_sw128(CUtensorMap* map, CUtensorMapDataType dtype, int elem_byt
                        const void* base, uint64_t inner, uint64_t outer,
                        uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer);
 
+// Same encoding without the descriptor cache: touches no host or device heap
+// (the caller owns `map`).
+int make_tmap_2d_sw128_uncached(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes,
+                                const void* base, uint64_t inner, uint64_t outer,
+                                uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer);
+
 }  // namespace ojx

@@ -117,6 +117,7 @@ _SIGS = {
     "ojx_ipc_close_handle": ([_P], ctypes.c_int),
     "ojx_gemm_allgather": ([ctypes.POINTER(GemmDesc), ctypes.POINTER(_P), ctypes.c_int32,
                             ctypes.c_int64, _P], ctypes.c_int),
+    "ojx_gemm_skinny_noalloc": ([ctypes.POINTER(GemmDesc), _P], ctypes.c_int),
     "ojx_debug_silence_producer_once": ([], ctypes.c_int),
 }
 
