@@ -33,7 +33,12 @@ constexpr int TC_BM = 128;
 constexpr int TC_THREADS = 320;  // 2 control warps + 8 epilogue warps
 constexpr int TC_EPI_WARPS = 8;
 
-template <int KIND, int BN, int STAGES>
+// Output tensor maps of the TMA-store epilogue: one per destination buffer.
+struct StoreMaps {
+  CUtensorMap m[OJX_MAX_PEERS];
+};
+
+template <int KIND, int BN, int STAGES, int STORE_TMA = 0>
 struct TcLayout {
   static constexpr int ELEM = KIND == 0 ? 2 : 4;
   static constexpr int BK = 128 / ELEM;  // elements in one 128-byte swizzle row
@@ -43,7 +48,10 @@ struct TcLayout {
   static constexpr int STAGE_BYTES = (A_BYTES + B_BYTES) * NPART;
   static constexpr uint32_t TMEM_COLS = 2 * BN;
   static constexpr int BAR_BYTES = 256;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
+  // TMA-store epilogue: one 32-row x 128-byte (swizzled) staging box per epilogue warp.
+  static constexpr int STAGE_OUT_BYTES = 32 * 128;
+  static constexpr int OUT_BYTES = STORE_TMA ? 8 * STAGE_OUT_BYTES : 0;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + OUT_BYTES + BAR_BYTES + 1024;
   static_assert(STAGE_BYTES % 1024 == 0, "stages must keep 1024-byte alignment");
   static_assert((2 * STAGES + 6) * 8 + 8 <= BAR_BYTES, "barrier area too small");
 };
@@ -130,19 +138,91 @@ __device__ __forceinline__ void store_row16(const EpiParams& ep, const uint32_t 
   }
 }
 
-template <int KIND, int FMT, int A_MN, int B_MN, int BN, int STAGES>
+// TMA-store epilogue of one 128-byte-wide chunk of a warp's 32 rows: TMEM ->
+// registers -> epilogue -> packed values in the warp's swizzled staging box ->
+// one tensor store per destination.  ESZ = output element bytes (chunk = 128/ESZ
+// columns).  `tcol` is the chunk's first TMEM column, `col0` its first output
+// column (relative to the destination maps), `row0` the box's first row.
+template <int ESZ>
+__device__ __forceinline__ void epi_chunk_tma(const EpiParams& ep, const StoreMaps& maps,
+                                              uint32_t tcol, int64_t row, int M, int col0, int N,
+                                              uint32_t stage, int lane, int row0) {
+  constexpr int V = 128 / ESZ;
+  float v[V];
+#pragma unroll
+  for (int i = 0; i < V / 16; ++i) {
+    uint32_t r[16];
+    tmem_ld16(tcol + i * 16, r);
+    tmem_wait_ld();
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[i * 16 + j] = __uint_as_float(r[j]);
+  }
+#pragma unroll
+  for (int i = 0; i < V / 16; ++i) {
+    float w[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) w[j] = v[i * 16 + j];
+    const int c = col0 + i * 16;
+    // rows past M are computed but never stored (the tensor store clips them);
+    // valid = 0 keeps their operand loads in bounds
+    epilogue16(ep, w, row, c, row < M ? max(0, min(16, N - c)) : 0);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[i * 16 + j] = w[j];
+  }
+  uint32_t packed[32];  // 128 bytes of this row
+  if (ESZ == 4) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) packed[j] = __float_as_uint(v[j]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      if (ep.dtype_c == OJX_BF16) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+        packed[j] = *reinterpret_cast<uint32_t*>(&h);
+      } else {
+        __half2 h = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+        packed[j] = *reinterpret_cast<uint32_t*>(&h);
+      }
+    }
+  }
+  // The previous chunk's stores must have finished reading the staging box.
+  if (lane == 0) bulk_wait_read_all();
+  __syncwarp();
+  const uint32_t rowaddr = stage + lane * 128;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const uint32_t a = rowaddr + ((j ^ (lane & 7)) << 4);  // 128-byte swizzle
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(packed[4 * j]),
+                 "r"(packed[4 * j + 1]), "r"(packed[4 * j + 2]), "r"(packed[4 * j + 3])
+                 : "memory");
+  }
+  fence_proxy_async_smem();  // generic-proxy writes -> visible to the TMA engine
+  __syncwarp();
+  if (lane == 0) {
+#pragma unroll
+    for (int d = 0; d < OJX_MAX_PEERS; ++d) {
+      if (d >= ep.n_dst) break;
+      tma_store_2d(&maps.m[d], stage, col0, row0);
+    }
+    bulk_commit_group();
+  }
+}
+
+template <int KIND, int FMT, int A_MN, int B_MN, int BN, int STAGES, int STORE_TMA>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmA2,
-                   const __grid_constant__ CUtensorMap tmB2, const EpiParams ep, const int M,
-                   const int N, const int K, const uint64_t budget, const int silence_producer) {
-  using L = TcLayout<KIND, BN, STAGES>;
+                   const __grid_constant__ CUtensorMap tmB2, const EpiParams ep,
+                   const __grid_constant__ StoreMaps smaps, const int M, const int N, const int K,
+                   const uint64_t budget, const int silence_producer) {
+  using L = TcLayout<KIND, BN, STAGES, STORE_TMA>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * L::STAGE_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * L::STAGE_BYTES + L::OUT_BYTES);
   volatile int* s_abort = reinterpret_cast<volatile int*>(bars + 2 * STAGES + 5);
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 6);
+  const uint32_t sout = smem_u32(smem + STAGES * L::STAGE_BYTES);  // staging boxes
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -293,17 +373,35 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const int n0 = nb * BN + half * (BN / 2);
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
                              static_cast<uint32_t>(acc * BN + half * (BN / 2));
+      if (STORE_TMA) {
+        const uint32_t stage_box = sout + static_cast<uint32_t>((warp - 2) * L::STAGE_OUT_BYTES);
+        const int row0 = mb * TC_BM + q * 32;
+        if (ep.dtype_c == OJX_F32) {
 #pragma unroll 1
-      for (int c = 0; c < BN / 2; c += 32) {
-        const int col0 = n0 + c;
-        if (col0 >= N) break;  // uniform across the warp
-        uint32_t r0[16], r1[16];
-        tmem_ld16(tbase + c, r0);
-        tmem_ld16(tbase + c + 16, r1);
-        tmem_wait_ld();
-        if (row < M) {
-          store_row16(ep, r0, row, col0, N);
-          if (col0 + 16 < N) store_row16(ep, r1, row, col0 + 16, N);
+          for (int c = 0; c < BN / 2; c += 32) {
+            if (n0 + c >= N) break;
+            epi_chunk_tma<4>(ep, smaps, tbase + c, row, M, n0 + c, N, stage_box, lane, row0);
+          }
+        } else {
+#pragma unroll 1
+          for (int c = 0; c < BN / 2; c += 64) {
+            if (n0 + c >= N) break;
+            epi_chunk_tma<2>(ep, smaps, tbase + c, row, M, n0 + c, N, stage_box, lane, row0);
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN / 2; c += 32) {
+          const int col0 = n0 + c;
+          if (col0 >= N) break;  // uniform across the warp
+          uint32_t r0[16], r1[16];
+          tmem_ld16(tbase + c, r0);
+          tmem_ld16(tbase + c + 16, r1);
+          tmem_wait_ld();
+          if (row < M) {
+            store_row16(ep, r0, row, col0, N);
+            if (col0 + 16 < N) store_row16(ep, r1, row, col0 + 16, N);
+          }
         }
       }
       tc_fence_before();
@@ -312,8 +410,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
-    // Stores into other GPUs' memory become visible system-wide before the
-    // kernel completes (the cross-rank barrier that follows relies on it).
+    // Every tensor store has completed (and, for stores into other GPUs' memory,
+    // is visible system-wide) before the kernel completes: the cross-rank barrier
+    // that follows an all-gathering GEMM relies on it.
+    if (STORE_TMA && lane == 0) bulk_wait_all();
+    __syncwarp();
     if (ep.n_dst > 1) __threadfence_system();
   }
 
@@ -399,22 +500,41 @@ EpiParams make_epi(const ojx_gemm_desc& d, const Dests* dests) {
   return ep;
 }
 
-template <int KIND, int FMT, int A_MN, int B_MN, int BN, int STAGES>
+template <int KIND, int FMT, int A_MN, int B_MN, int BN, int STAGES, int STORE_TMA>
 static int run_tc(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& a2,
-                  const CUtensorMap& b2, const EpiParams& ep, int M, int N, int K,
-                  cudaStream_t s) {
-  using L = TcLayout<KIND, BN, STAGES>;
-  auto kern = tc_gemm_kernel<KIND, FMT, A_MN, B_MN, BN, STAGES>;
+                  const CUtensorMap& b2, const EpiParams& ep, const StoreMaps& sm, int M, int N,
+                  int K, cudaStream_t s) {
+  using L = TcLayout<KIND, BN, STAGES, STORE_TMA>;
+  auto kern = tc_gemm_kernel<KIND, FMT, A_MN, B_MN, BN, STAGES, STORE_TMA>;
   int st = ensure_smem_attr(reinterpret_cast<const void*>(kern), L::SMEM_BYTES);
   if (st) return st;
   const DeviceProps& p = current_props();
   const long tiles = static_cast<long>((M + TC_BM - 1) / TC_BM) * ((N + BN - 1) / BN);
   const int grid = static_cast<int>(std::min<long>(tiles, p.sm_count));
   const int silence = g_silence_producer_once.exchange(0);
-  kern<<<grid, TC_THREADS, L::SMEM_BYTES, s>>>(a, b, a2, b2, ep, M, N, K, g_wait_budget.load(),
+  kern<<<grid, TC_THREADS, L::SMEM_BYTES, s>>>(a, b, a2, b2, ep, sm, M, N, K, g_wait_budget.load(),
                                                silence);
   g_launches.fetch_add(1);
   return cuda_status(cudaGetLastError(), "tc_gemm launch");
+}
+
+// Output tensor maps for the TMA-store epilogue: destination i is the [M, N] block
+// at ep.dst[i] + col_offset with row stride ldc.  Returns false (no error) when an
+// address or the stride is not 16-byte aligned; the register-store epilogue is
+// used then.
+static bool make_store_maps(const EpiParams& ep, int M, int N, StoreMaps* sm) {
+  const int esz = ep.dtype_c == OJX_F32 ? 4 : 2;
+  if ((ep.ldc * esz) % 16 != 0 || (ep.col_offset * esz) % 16 != 0) return false;
+  const CUtensorMapDataType dt = ep.dtype_c == OJX_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : ep.dtype_c == OJX_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                          : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  for (int i = 0; i < ep.n_dst; ++i) {
+    const char* base = static_cast<const char*>(ep.dst[i]) + ep.col_offset * esz;
+    if (reinterpret_cast<uintptr_t>(base) % 16 != 0) return false;
+    if (make_tmap_2d_sw128(&sm->m[i], dt, esz, base, N, M, ep.ldc * esz, 128 / esz, 32) != OJX_OK)
+      return false;
+  }
+  return true;
 }
 
 bool tc_gemm_supported(const ojx_gemm_desc& d) {
@@ -448,11 +568,14 @@ int launch_tc_gemm(const ojx_gemm_desc& d, cudaStream_t s, const Dests* dests) {
     st = make_tmap_2d_sw128(&tb, tdt, 2, d.b, K, N, d.ldb * 2, 64, BN);
   if (st) return st;
   const EpiParams ep = make_epi(d, dests);
+  StoreMaps sm;
+  const bool tma_out = make_store_maps(ep, M, N, &sm);
   const bool bf = d.dtype_a == OJX_BF16;
   const int am = d.trans_a ? 1 : 0, bm = d.trans_b ? 0 : 1;
 #define OJX_TC_CASE(FMTV, AMN, BMN, BNV)                                                  \
   if ((bf ? 1 : 0) == FMTV && am == AMN && bm == BMN && BN == BNV)                         \
-    return run_tc<0, FMTV, AMN, BMN, BNV, BNV == 256 ? 4 : 6>(ta, tb, ta, tb, ep, M, N, K, s);
+    return tma_out ? run_tc<0, FMTV, AMN, BMN, BNV, BNV == 256 ? 4 : 6, 1>(ta, tb, ta, tb, ep, sm, M, N, K, s) \
+                   : run_tc<0, FMTV, AMN, BMN, BNV, BNV == 256 ? 4 : 6, 0>(ta, tb, ta, tb, ep, sm, M, N, K, s);
 #define OJX_TC_BN(FMTV, AMN, BMN) \
   OJX_TC_CASE(FMTV, AMN, BMN, 256) OJX_TC_CASE(FMTV, AMN, BMN, 128)
   OJX_TC_BN(1, 0, 1) OJX_TC_BN(1, 0, 0) OJX_TC_BN(1, 1, 1) OJX_TC_BN(1, 1, 0)
@@ -491,7 +614,11 @@ int launch_tc_gemm_3xtf32(const ojx_gemm_desc& d, cudaStream_t s) {
   if ((st = make_tmap_2d_sw128(&ta2, F, 4, a_lo, Kp, M, Kp * 4ull, 32, 128))) return st;
   if ((st = make_tmap_2d_sw128(&tb, F, 4, b_hi, Kp, N, Kp * 4ull, 32, BN))) return st;
   if ((st = make_tmap_2d_sw128(&tb2, F, 4, b_lo, Kp, N, Kp * 4ull, 32, BN))) return st;
-  return run_tc<1, 2, 0, 0, BN, 3>(ta, tb, ta2, tb2, make_epi(d), M, N, Kp, s);
+  const EpiParams ep = make_epi(d);
+  StoreMaps sm;
+  if (make_store_maps(ep, M, N, &sm))
+    return run_tc<1, 2, 0, 0, BN, 3, 1>(ta, tb, ta2, tb2, ep, sm, M, N, Kp, s);
+  return run_tc<1, 2, 0, 0, BN, 3, 0>(ta, tb, ta2, tb2, ep, sm, M, N, Kp, s);
 }
 
 }  // namespace ojx
