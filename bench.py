@@ -304,7 +304,7 @@ def run_ours(args, cfg, world, rank, local):
         # 3xTF32 runs three tf32 MMAs (half the bf16 rate each) per fp32 multiply-add
         peak = peak / 2 / 3
     roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-            "frac": achieved / peak, "traffic": _traffic(args.config, route),
+            "frac": achieved / peak, "traffic": _traffic(args),
             "kernel": f"ojx route {route}", "peak_source": f"{peak_kind} "
             f"{'bf16_tflops_sustained' if sustained else 'bf16_tflops'}"
             f"{' / 6 (3xTF32 effective)' if code == L.F32 else ''}",
@@ -383,12 +383,14 @@ def e2e_measure(args, lib, L, A, C, M, K, N, es, gemm, gather, world, dev, strea
             "note": "C-ABI with pinned host buffers; CUDA events on the launching stream, max over ranks"}
 
 
-def _traffic(config: str, route: str):
-    """DRAM bytes per launch from the committed ncu summary, when one exists."""
+def _traffic(args):
+    """DRAM bytes per launch of the dominant kernel, from the committed ncu summaries
+    (profiles/traffic.json), or None when that workload was not captured."""
+    key = args.config + (f"@{args.size}" if args.size else "") + (f"@m{args.m}" if args.m else "")
     p = REPO / "profiles" / "traffic.json"
     if p.exists():
         try:
-            return json.loads(p.read_text()).get(config)
+            return json.loads(p.read_text()).get(key)
         except Exception:
             return None
     return None
