@@ -247,6 +247,46 @@ int ojx_gemm_allgather(const ojx_gemm_desc* d, void* const* c_peers, int32_t n_p
  * the array up; make it before capturing a stream. */
 int ojx_gemm_skinny_noalloc(const ojx_gemm_desc* d, ojx_stream s);
 
+/* ── graph capture and replay ──────────────────────────────────────────────
+ * Replaces torchcl/jit/graph_runner.py: `capture_graph` (:70-86) records the
+ * launches made inside a `with` block and `CapturedGraph.replay` (:58-62)
+ * re-submits them.  Here the recording is a CUDA stream capture of every ojx
+ * launch issued on `s` between begin and end, instantiated once into a CUDA
+ * graph that one cudaGraphLaunch replays.  Launches that need scratch (the 3xTF32
+ * operand split, the skinny route's partial sums and arrival counters) get
+ * buffers owned by the graph, freed by ojx_graph_destroy.  `s` must be a stream
+ * from ojx_stream_create (the legacy stream cannot be captured); the capture uses
+ * cudaStreamCaptureModeRelaxed so the buffer pool may grow during it.  Between
+ * begin and end nothing on `s` executes: synchronising `s` or reading results
+ * back fails and invalidates the capture. */
+typedef struct ojx_graph_s* ojx_graph;
+
+enum { OJX_NODE_OTHER = 0, OJX_NODE_KERNEL = 1, OJX_NODE_MEMSET = 2, OJX_NODE_MEMCPY = 3 };
+
+/* One recorded node: graph_runner.py:25-32 RecordedCommand (kernel, global and
+ * local size).  `name` is the kernel's name without template arguments. */
+typedef struct ojx_graph_node {
+  int32_t type;
+  int32_t grid[3];
+  int32_t block[3];
+  int32_t smem_bytes;
+  char name[128];
+} ojx_graph_node;
+
+int ojx_graph_capture_begin(ojx_stream s);
+/* Ends the capture on `s` and instantiates it.  On failure (e.g. the capture was
+ * invalidated) the partial graph and its buffers are released. */
+int ojx_graph_capture_end(ojx_stream s, ojx_graph* g);
+/* Launches the whole recorded sequence on `s` (any stream of the same device). */
+int ojx_graph_launch(ojx_graph g, ojx_stream s);
+/* Waits for the device, then frees the graph and the buffers it owns. */
+int ojx_graph_destroy(ojx_graph g);
+/* Number of nodes (graph_runner.py:64-65 __len__ counts kernel launches: pass
+ * kernels_only = 1 for that count). */
+int ojx_graph_node_count(ojx_graph g, int kernels_only, int32_t* n);
+/* Node `index` (0-based, in execution order). */
+int ojx_graph_node_get(ojx_graph g, int32_t index, ojx_graph_node* out);
+
 /* Test hook: the next ojx_gemm on a tcgen05 route runs with its TMA producer
  * silenced, so the MMA warp's bounded wait must expire and the kernel must
  * return with OJX_ERR_TIMEOUT recorded (read it with ojx_poll_device_error). */

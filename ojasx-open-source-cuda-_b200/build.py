@@ -2,8 +2,8 @@
 
     python ojasx-open-source-cuda-_b200/build.py [--verbose-ptxas]
 
-Compiles csrc/ojx_kernels.cu (every kernel, one translation unit), csrc/runtime.cpp
-and csrc/tmap.cpp with nvcc for `-gencode arch=compute_100a,code=sm_100a` and links
+Compiles csrc/ojx_kernels.cu (every kernel, one translation unit), csrc/runtime.cpp,
+csrc/tmap.cpp and csrc/graph.cpp with nvcc for `-gencode arch=compute_100a,code=sm_100a` and links
 them into ojasx-open-source-cuda-_b200/torchcl/_lib/libojx.so, next to the Python
 package that loads it.  The CUDA runtime is linked statically, so the library does
 not depend on which libcudart another module (e.g. torch) already loaded.
@@ -27,7 +27,7 @@ LIB = OUT_DIR / "libojx.so"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-O3", f"-I{INCLUDE}", f"-I{CSRC}"]
-SOURCES = ["ojx_kernels.cu", "runtime.cpp", "tmap.cpp"]
+SOURCES = ["ojx_kernels.cu", "runtime.cpp", "tmap.cpp", "graph.cpp"]
 
 
 def nvcc() -> str:

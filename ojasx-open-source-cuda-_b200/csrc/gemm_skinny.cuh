@@ -20,7 +20,10 @@
 //
 // Scratch per call: partial slots  groups * max_contributors * SK_TPU*16*128 fp32,
 // and one 64-bit arrival counter per group holding (launch epoch << 32 | count),
-// so stale counts from an earlier (or aborted) launch never need resetting.
+// so stale counts from an earlier (or aborted) launch never need resetting.  The
+// last arriver also stores 0 into its counter, so a completed launch leaves the
+// counters as it found them: a launch replayed from a CUDA graph (same epoch
+// every time) then starts from zero as well.
 #include <cuda_runtime.h>
 #include <algorithm>
 #include "sm100.cuh"
@@ -283,7 +286,10 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
             old = seen;
           }
           *s_last = (count == static_cast<unsigned int>(ncontrib)) ? 1 : 0;
-          if (*s_last) __threadfence();
+          if (*s_last) {
+            *ctr = 0ull;  // every contributor of this group has arrived
+            __threadfence();
+          }
         }
         named_bar_sync(1, 128);
         finish = *s_last != 0;
@@ -402,10 +408,10 @@ int launch_skinny_gemm(const ojx_gemm_desc& d, cudaStream_t s, const Dests* dest
   p.maxc = skinny_max_contrib(p.n_groups, p.KB, p.U, p.G);
   const size_t part_bytes = static_cast<size_t>(p.n_groups) * p.maxc * SK_SLOT * 4;
   p.partials = static_cast<float*>(stream_workspace(s, part_bytes, 1, false));
-  if (!p.partials) return OJX_ERR_OOM;
+  if (!p.partials) return workspace_error();
   p.counters = static_cast<unsigned long long*>(
       stream_workspace(s, static_cast<size_t>(p.n_groups) * 8, 2, /*zero=*/true));
-  if (!p.counters) return OJX_ERR_OOM;
+  if (!p.counters) return workspace_error();
   p.epoch = g_skinny_epoch.fetch_add(1);
   if (p.epoch == 0) p.epoch = g_skinny_epoch.fetch_add(1);
   p.budget = g_wait_budget.load();

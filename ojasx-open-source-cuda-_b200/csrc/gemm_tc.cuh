@@ -592,7 +592,7 @@ int launch_tc_gemm_3xtf32(const ojx_gemm_desc& d, cudaStream_t s) {
   const size_t a_part = al(static_cast<size_t>(M) * Kp * 4);
   const size_t b_part = al(static_cast<size_t>(N) * Kp * 4);
   char* ws = static_cast<char*>(stream_workspace(s, 2 * a_part + 2 * b_part, 0, false));
-  if (!ws) return OJX_ERR_OOM;
+  if (!ws) return workspace_error();
   float* a_hi = reinterpret_cast<float*>(ws);
   float* a_lo = reinterpret_cast<float*>(ws + a_part);
   float* b_hi = reinterpret_cast<float*>(ws + 2 * a_part);

@@ -10,6 +10,8 @@ namespace ojx {
 
 // Thread-local error message; returns `code` so call sites can `return set_error(...)`.
 int set_error(int code, const char* fmt, ...);
+// Code passed to this thread's last set_error.
+int last_error_code();
 // OJX_OK if e == cudaSuccess, else records the CUDA error string and returns OJX_ERR_CUDA
 // (OJX_ERR_OOM for cudaErrorMemoryAllocation).
 int cuda_status(cudaError_t e, const char* what);
@@ -32,7 +34,12 @@ const DeviceProps& current_props();
 // process.  slot selects one of several independent buffers per stream.  With
 // `zero`, a freshly (re)allocated buffer is cleared on the stream.  Returns
 // nullptr and sets the error on failure.
+// While `s` is being captured into a graph (ojx_graph_capture_begin), every call
+// returns a fresh buffer owned by that capture instead (capture_workspace).
 void* stream_workspace(cudaStream_t s, size_t bytes, int slot, bool zero);
+void* capture_workspace(cudaStream_t s, size_t bytes, bool zero);
+// Status code of this thread's last failed stream_workspace call.
+int workspace_error();
 
 // cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (kernel, device).
 int ensure_smem_attr(const void* kernel, int bytes);

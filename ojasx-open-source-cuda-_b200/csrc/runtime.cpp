@@ -19,6 +19,7 @@
 namespace ojx {
 
 static thread_local std::string t_last_error;
+static thread_local int t_last_code = OJX_OK;
 static thread_local int t_last_route = OJX_ROUTE_NONE;
 std::atomic<uint64_t> g_launches{0};
 std::atomic<uint64_t> g_wait_budget{4000000000ull};  // about 2 s at B200 clocks
@@ -31,8 +32,11 @@ int set_error(int code, const char* fmt, ...) {
   vsnprintf(buf, sizeof(buf), fmt, ap);
   va_end(ap);
   t_last_error = buf;
+  t_last_code = code;
   return code;
 }
+
+int last_error_code() { return t_last_code; }
 
 int cuda_status(cudaError_t e, const char* what) {
   if (e == cudaSuccess) return OJX_OK;
@@ -225,7 +229,13 @@ struct WsBuf {
   size_t bytes = 0;
 };
 
-void* stream_workspace(cudaStream_t s, size_t bytes, int slot, bool zero) {
+static thread_local int t_ws_error = OJX_OK;
+int workspace_error() { return t_ws_error == OJX_OK ? OJX_ERR_OOM : t_ws_error; }
+
+static void* stream_workspace_impl(cudaStream_t s, size_t bytes, int slot, bool zero) {
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (s && cudaStreamIsCapturing(s, &cs) == cudaSuccess && cs != cudaStreamCaptureStatusNone)
+    return capture_workspace(s, bytes, zero);
   static std::mutex mu;
   static std::map<WsKey, WsBuf>* bufs = new std::map<WsKey, WsBuf>();
   int dev = 0;
@@ -258,6 +268,15 @@ void* stream_workspace(cudaStream_t s, size_t bytes, int slot, bool zero) {
   }
   w.p = p;
   w.bytes = nb;
+  return p;
+}
+
+void* stream_workspace(cudaStream_t s, size_t bytes, int slot, bool zero) {
+  void* p = stream_workspace_impl(s, bytes, slot, zero);
+  if (!p) {
+    // set_error has recorded the message; keep its code for the caller.
+    t_ws_error = last_error_code();
+  }
   return p;
 }
 

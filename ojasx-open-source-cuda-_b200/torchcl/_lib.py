@@ -71,6 +71,14 @@ class PoolStats(ctypes.Structure):
         "peak_bytes", "total_allocated_bytes", "active_buffers", "evictions")]
 
 
+class GraphNode(ctypes.Structure):
+    _fields_ = [("type", ctypes.c_int32), ("grid", ctypes.c_int32 * 3),
+                ("block", ctypes.c_int32 * 3), ("smem_bytes", ctypes.c_int32),
+                ("name", ctypes.c_char * 128)]
+
+
+NODE_TYPES = {0: "other", 1: "kernel", 2: "memset", 3: "memcpy"}
+
 _P = ctypes.c_void_p
 _SIGS = {
     "ojx_abi_version": ([], ctypes.c_int),
@@ -118,6 +126,12 @@ _SIGS = {
     "ojx_gemm_allgather": ([ctypes.POINTER(GemmDesc), ctypes.POINTER(_P), ctypes.c_int32,
                             ctypes.c_int64, _P], ctypes.c_int),
     "ojx_gemm_skinny_noalloc": ([ctypes.POINTER(GemmDesc), _P], ctypes.c_int),
+    "ojx_graph_capture_begin": ([_P], ctypes.c_int),
+    "ojx_graph_capture_end": ([_P, ctypes.POINTER(_P)], ctypes.c_int),
+    "ojx_graph_launch": ([_P, _P], ctypes.c_int),
+    "ojx_graph_destroy": ([_P], ctypes.c_int),
+    "ojx_graph_node_count": ([_P, ctypes.c_int, ctypes.POINTER(ctypes.c_int32)], ctypes.c_int),
+    "ojx_graph_node_get": ([_P, ctypes.c_int32, ctypes.POINTER(GraphNode)], ctypes.c_int),
     "ojx_debug_silence_producer_once": ([], ctypes.c_int),
 }
 

@@ -35,7 +35,7 @@ import torch
 from torchcl import _lib as L
 from torchcl.ops.engine import get_engine, ojx_dtype
 from torchcl.runtime.context import synchronize as _sync
-from torchcl.runtime.memory import CLBuffer, get_buffer_pool
+from torchcl.runtime.memory import CLBuffer, get_buffer_pool, note_use
 
 _opencl_buffers = weakref.WeakValueDictionary()
 _buffer_lock = threading.RLock()
@@ -111,11 +111,12 @@ def _get_buf(tensor) -> CLBuffer:
     if tid is not None:
         with _buffer_lock:
             buf = _opencl_buffers.get(tid)
-        if buf is not None:
-            return buf
-        if _is_lazy(e):
+        if buf is None and _is_lazy(e):
             materialize_lazy_tensor(e)
-            return _opencl_buffers[tid]
+            buf = _opencl_buffers[tid]
+        if buf is not None:
+            note_use(buf)  # a graph being captured must keep this buffer
+            return buf
     raise ValueError(_NOT_ON_DEVICE)
 
 
@@ -140,6 +141,11 @@ def is_opencl_tensor(tensor: Any) -> bool:
 
 # ── lazy nodes ───────────────────────────────────────────────────────────
 
+# Lazy nodes created while a graph is captured (weak references, creation order);
+# torchcl.jit.graph_runner materialises the live ones before the capture ends.
+_capture_lazy: list | None = None
+
+
 def _new_lazy(shape, dtype, op_type: str, inputs: list, **attrs):
     handle, _ = _make_handle(shape, dtype)
     handle._lazy_inputs = inputs
@@ -147,6 +153,8 @@ def _new_lazy(shape, dtype, op_type: str, inputs: list, **attrs):
     handle._lazy_ops = list(attrs.pop("ops", []))
     for k, v in attrs.items():
         setattr(handle, k, v)
+    if _capture_lazy is not None:
+        _capture_lazy.append(weakref.ref(handle))
     return _wrap(handle)
 
 

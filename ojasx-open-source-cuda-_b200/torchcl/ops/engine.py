@@ -16,7 +16,7 @@ import torch
 
 from torchcl import _lib as L
 from torchcl.runtime.context import get_queue
-from torchcl.runtime.memory import CLBuffer, get_buffer_pool
+from torchcl.runtime.memory import CLBuffer, get_buffer_pool, note_use
 
 _TORCH_TO_OJX = {torch.float32: L.F32, torch.bfloat16: L.BF16, torch.float16: L.F16}
 _OJX_TO_TORCH = {v: k for k, v in _TORCH_TO_OJX.items()}
@@ -176,6 +176,7 @@ def _addr(buf) -> int | None:
     if buf is None:
         return None
     if isinstance(buf, CLBuffer):
+        note_use(buf)  # a graph being captured must keep this buffer
         return buf.buffer
     return int(buf)
 

@@ -111,9 +111,21 @@ def _get_default_queue() -> int:
     return _default_stream
 
 
+# True while torchcl.jit.graph_runner.capture_graph records launches: nothing
+# executes then, so waiting for results (synchronize, downloads) is an error.
+_capture_active = False
+
+
+def check_not_capturing(what: str) -> None:
+    if _capture_active:
+        raise RuntimeError(f"{what} is not allowed while a graph is being captured: upload inputs "
+                           "before capture_graph() and read results after its `with` block")
+
+
 def synchronize() -> None:
     """Block until all work on the current stream (and the default queue) finished."""
     _ensure_initialized()
+    check_not_capturing("synchronize")
     lib = L.lib()
     q = get_queue()
     L.check(lib.ojx_stream_synchronize(q), "synchronize")

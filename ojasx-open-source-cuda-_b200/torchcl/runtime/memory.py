@@ -17,7 +17,8 @@ import numpy as np
 import torch
 
 from torchcl import _lib as L
-from torchcl.runtime.context import _ensure_initialized, get_queue
+from torchcl.runtime import context as _ctx
+from torchcl.runtime.context import _ensure_initialized, check_not_capturing, get_queue
 
 
 def _next_power_of_two(n: int) -> int:
@@ -69,6 +70,73 @@ def _host_view(arr) -> tuple[int, int, Any]:
     return a.ctypes.data, a.nbytes, a
 
 
+# ── graph capture bookkeeping ─────────────────────────────────────────────
+# A captured graph replays launches on fixed device addresses.  While a capture is
+# active every buffer allocated or handed to a launch is recorded; when it ends the
+# graph pins those addresses, and freeing a pinned buffer is deferred until the
+# last graph that uses it is destroyed, so a replay never writes into memory the
+# pool has handed out again.  Frees requested during the capture are deferred too.
+_cap_lock = threading.RLock()
+_capture_sink: dict[int, CLBuffer] | None = None
+_pins: dict[int, int] = {}
+_deferred: dict[int, "CLBuffer"] = {}
+
+
+def note_use(buf) -> None:
+    """Record `buf` as used by the graph being captured (no-op otherwise)."""
+    if _capture_sink is not None and isinstance(buf, CLBuffer):
+        with _cap_lock:
+            if _capture_sink is not None:
+                _capture_sink[buf.buffer] = buf
+
+
+def begin_capture() -> None:
+    global _capture_sink
+    with _cap_lock:
+        if _capture_sink is not None:
+            raise RuntimeError("a graph capture is already active")
+        _capture_sink = {}
+        _ctx._capture_active = True
+
+
+def end_capture(keep: bool) -> list[int]:
+    """Close the capture; pin its buffers if `keep`.  Returns the pinned addresses."""
+    global _capture_sink
+    with _cap_lock:
+        sink, _capture_sink = _capture_sink or {}, None
+        _ctx._capture_active = False
+        addrs = sorted(sink) if keep else []
+        for a in addrs:
+            _pins[a] = _pins.get(a, 0) + 1
+        pending = [a for a in list(_deferred) if a not in _pins]
+    for a in pending:
+        _really_free(a)
+    return addrs
+
+
+def release_pins(addrs) -> None:
+    """A graph using `addrs` was destroyed: finish the frees it deferred."""
+    ready = []
+    with _cap_lock:
+        for a in addrs:
+            n = _pins.get(a, 0) - 1
+            if n > 0:
+                _pins[a] = n
+                continue
+            _pins.pop(a, None)
+            if a in _deferred and _capture_sink is None:
+                ready.append(a)
+    for a in ready:
+        _really_free(a)
+
+
+def _really_free(addr: int) -> None:
+    with _cap_lock:
+        buf = _deferred.pop(addr, None)
+    if buf is not None:
+        L.check(L.lib().ojx_free(addr), "free")
+
+
 class CLBufferPool:
     """Caching device allocator facade (memory.py:61-203)."""
 
@@ -86,6 +154,7 @@ class CLBufferPool:
         buf = CLBuffer(p.value, int(nbytes), cap.value, dtype, shape, is_pinned=pin_memory)
         with self._lock:
             self._active[buf._id] = buf
+        note_use(buf)
         return buf
 
     def free(self, cl_buf: CLBuffer) -> None:
@@ -94,6 +163,10 @@ class CLBufferPool:
         cl_buf._freed = True
         with self._lock:
             self._active.pop(cl_buf._id, None)
+        with _cap_lock:
+            if _capture_sink is not None or cl_buf.buffer in _pins:
+                _deferred[cl_buf.buffer] = cl_buf  # a graph may still use it
+                return
         L.check(L.lib().ojx_free(cl_buf.buffer), "free")
 
     def empty_cache(self) -> None:
@@ -102,6 +175,7 @@ class CLBufferPool:
     def host_to_device(self, host_array, cl_buf: CLBuffer | None = None,
                        non_blocking: bool = False) -> CLBuffer:
         """Copy a host numpy array (or CPU torch tensor) into a (new) device buffer."""
+        check_not_capturing("host_to_device")
         addr, nbytes, keep = _host_view(host_array)
         if cl_buf is None:
             dtype = keep.dtype
@@ -122,6 +196,7 @@ class CLBufferPool:
         return out
 
     def copy_to_host(self, cl_buf: CLBuffer, host_addr: int, nbytes: int) -> None:
+        check_not_capturing("device_to_host")
         q = get_queue()
         L.check(L.lib().ojx_memcpy_d2h(host_addr, cl_buf.buffer, nbytes, q), "device_to_host")
         L.check(L.lib().ojx_stream_synchronize(q), "device_to_host sync")
@@ -130,10 +205,13 @@ class CLBufferPool:
     def device_to_device(self, src: CLBuffer, dst: CLBuffer | None = None) -> CLBuffer:
         if dst is None:
             dst = self.allocate(src.nbytes, src.dtype, src.shape)
+        note_use(src)
+        note_use(dst)
         L.check(L.lib().ojx_memcpy_d2d(dst.buffer, src.buffer, src.nbytes, get_queue()), "d2d")
         return dst
 
     def zero_fill(self, cl_buf: CLBuffer) -> None:
+        note_use(cl_buf)
         L.check(L.lib().ojx_memset(cl_buf.buffer, 0, cl_buf.nbytes, get_queue()), "zero_fill")
 
     def get_stats(self) -> dict[str, Any]:
