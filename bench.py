@@ -304,6 +304,9 @@ def run_ours(args, cfg, world, rank, local):
            torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     launches0 = lib.ojx_kernel_launch_count()
     with ClockSampler(local) as clk:
+        # Keep the GPU busy while the host queues the timed steps, so that the
+        # per-step events measure device time, not the host's launch latency.
+        torch.cuda._sleep(int(1e6 + 2e5 * args.steps))
         for i in range(args.steps):
             if needs_flush:
                 flush.zero_()

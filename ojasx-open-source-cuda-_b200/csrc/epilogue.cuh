@@ -112,6 +112,73 @@ __device__ __forceinline__ float epilogue_value(const EpiParams& ep, float acc, 
   return v;
 }
 
+// ── 8-wide row pieces with 16-byte accesses ────────────────────────────────
+
+// x[0..7] = p[i0 .. i0+7]; only the first `valid` are read (the rest are 0).
+// 16-byte vector loads when the whole piece is inside and aligned.
+__device__ __forceinline__ void load8(const void* p, int dtype, int64_t i0, int valid,
+                                      float (&x)[8]) {
+  const int esz = dtype == OJX_F32 ? 4 : 2;
+  const char* src = static_cast<const char*>(p) + i0 * esz;
+  if (valid >= 8 && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+    if (dtype == OJX_F32) {
+      const float4 a = __ldg(reinterpret_cast<const float4*>(src));
+      const float4 b = __ldg(reinterpret_cast<const float4*>(src) + 1);
+      x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+      x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+    } else {
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(src));
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        if (dtype == OJX_BF16) {
+          const __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&w[k]);
+          x[2 * k] = __low2float(h);
+          x[2 * k + 1] = __high2float(h);
+        } else {
+          const __half2 h = *reinterpret_cast<const __half2*>(&w[k]);
+          x[2 * k] = __low2float(h);
+          x[2 * k + 1] = __high2float(h);
+        }
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) x[j] = j < valid ? load_elem(p, i0 + j, dtype) : 0.0f;
+  }
+}
+
+// p[i0 .. i0+7] = v (only the first `valid`): one 16-byte store for 16-bit
+// types (two for fp32) when the whole piece is inside and aligned.
+__device__ __forceinline__ void store8(void* p, int dtype, int64_t i0, int valid,
+                                       const float (&v)[8]) {
+  const int esz = dtype == OJX_F32 ? 4 : 2;
+  char* dst = static_cast<char*>(p) + i0 * esz;
+  if (valid >= 8 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+    if (dtype == OJX_F32) {
+      reinterpret_cast<float4*>(dst)[0] = make_float4(v[0], v[1], v[2], v[3]);
+      reinterpret_cast<float4*>(dst)[1] = make_float4(v[4], v[5], v[6], v[7]);
+    } else {
+      uint32_t w[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        if (dtype == OJX_BF16) {
+          const __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * k], v[2 * k + 1]);
+          w[k] = *reinterpret_cast<const uint32_t*>(&h);
+        } else {
+          const __half2 h = __floats2half2_rn(v[2 * k], v[2 * k + 1]);
+          w[k] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+      }
+      *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (j < valid) store_elem(p, i0 + j, dtype, v[j]);
+  }
+}
+
 // ── 16-wide variants: one dispatch per 16 consecutive columns of a row ─────────
 
 // x[0..15] = p[i0 .. i0+15] (only the first `valid` when the row ends early).
@@ -153,45 +220,72 @@ __device__ __forceinline__ void load16(const void* p, int dtype, int64_t i0, int
   }
 }
 
-__device__ __forceinline__ void unary16(int op, float (&v)[16]) {
-#define OJX_U16(EXPR)                                         \
-  _Pragma("unroll") for (int j = 0; j < 16; ++j) {            \
+// v[j] = op(v[j]) for N values: one dispatch for the whole vector.
+template <int N>
+__device__ __forceinline__ void unary_n(int op, float (&v)[N]) {
+#define OJX_UN(EXPR)                                          \
+  _Pragma("unroll") for (int j = 0; j < N; ++j) {             \
     const float x = v[j];                                     \
     v[j] = (EXPR);                                            \
   }                                                           \
   break;
   switch (op) {
-    case OJX_UN_RELU: OJX_U16(fmaxf(x, 0.0f))
-    case OJX_UN_SIGMOID: OJX_U16(__fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x))))
-    case OJX_UN_TANH: OJX_U16(tanhf(x))
-    case OJX_UN_NEG: OJX_U16(-x)
-    case OJX_UN_ABS: OJX_U16(fabsf(x))
-    case OJX_UN_EXP: OJX_U16(expf(x))
-    case OJX_UN_LOG: OJX_U16(logf(x))
-    case OJX_UN_SQRT: OJX_U16(__fsqrt_rn(x))
-    case OJX_UN_SILU: OJX_U16(__fdiv_rn(x, __fadd_rn(1.0f, expf(-x))))
-    case OJX_UN_GELU: OJX_U16(apply_unary(OJX_UN_GELU, x))
-    case OJX_UN_SQUARE: OJX_U16(__fmul_rn(x, x))
+    case OJX_UN_RELU: OJX_UN(fmaxf(x, 0.0f))
+    case OJX_UN_SIGMOID: OJX_UN(__fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x))))
+    case OJX_UN_TANH: OJX_UN(tanhf(x))
+    case OJX_UN_NEG: OJX_UN(-x)
+    case OJX_UN_ABS: OJX_UN(fabsf(x))
+    case OJX_UN_EXP: OJX_UN(expf(x))
+    case OJX_UN_LOG: OJX_UN(logf(x))
+    case OJX_UN_SQRT: OJX_UN(__fsqrt_rn(x))
+    case OJX_UN_SILU: OJX_UN(__fdiv_rn(x, __fadd_rn(1.0f, expf(-x))))
+    case OJX_UN_GELU: OJX_UN(apply_unary(OJX_UN_GELU, x))
+    case OJX_UN_SQUARE: OJX_UN(__fmul_rn(x, x))
     default: break;
   }
-#undef OJX_U16
+#undef OJX_UN
 }
 
-__device__ __forceinline__ void binary16(int op, bool lhs, float (&v)[16], const float (&x)[16]) {
-#define OJX_B16(EXPR)                                         \
-  _Pragma("unroll") for (int j = 0; j < 16; ++j) {            \
+__device__ __forceinline__ void unary16(int op, float (&v)[16]) { unary_n<16>(op, v); }
+
+// unary_n for results that are rounded to bf16/fp16 afterwards: the logistic
+// ops divide with __fdividef and exponentiate with __expf (errors of a few fp32
+// ulp, far below 16-bit precision) instead of the correctly rounded division,
+// which costs several hundred cycles per value.  Every other op is unary_n's.
+template <int N>
+__device__ __forceinline__ void unary_n_half(int op, float (&v)[N]) {
+  if (op == OJX_UN_SILU) {
+#pragma unroll
+    for (int j = 0; j < N; ++j) v[j] = __fdividef(v[j], 1.0f + __expf(-v[j]));
+  } else if (op == OJX_UN_SIGMOID) {
+#pragma unroll
+    for (int j = 0; j < N; ++j) v[j] = __fdividef(1.0f, 1.0f + __expf(-v[j]));
+  } else {
+    unary_n<N>(op, v);
+  }
+}
+
+// v[j] = v[j] op x[j] (x[j] op v[j] when lhs) for N values.
+template <int N>
+__device__ __forceinline__ void binary_n(int op, bool lhs, float (&v)[N], const float (&x)[N]) {
+#define OJX_BN(EXPR)                                          \
+  _Pragma("unroll") for (int j = 0; j < N; ++j) {             \
     const float a = lhs ? x[j] : v[j], b = lhs ? v[j] : x[j]; \
     v[j] = (EXPR);                                            \
   }                                                           \
   break;
   switch (op) {
-    case OJX_BIN_ADD: OJX_B16(__fadd_rn(a, b))
-    case OJX_BIN_SUB: OJX_B16(__fsub_rn(a, b))
-    case OJX_BIN_MUL: OJX_B16(__fmul_rn(a, b))
-    case OJX_BIN_DIV: OJX_B16(__fdiv_rn(a, b))
+    case OJX_BIN_ADD: OJX_BN(__fadd_rn(a, b))
+    case OJX_BIN_SUB: OJX_BN(__fsub_rn(a, b))
+    case OJX_BIN_MUL: OJX_BN(__fmul_rn(a, b))
+    case OJX_BIN_DIV: OJX_BN(__fdiv_rn(a, b))
     default: break;
   }
-#undef OJX_B16
+#undef OJX_BN
+}
+
+__device__ __forceinline__ void binary16(int op, bool lhs, float (&v)[16], const float (&x)[16]) {
+  binary_n<16>(op, lhs, v, x);
 }
 
 // Epilogue of 16 consecutive columns col0.. of one row (valid = columns < N).

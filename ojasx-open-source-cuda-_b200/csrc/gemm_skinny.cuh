@@ -45,7 +45,9 @@ constexpr int SK_STAGE_BYTES = SK_W_BYTES + SK_X_BYTES;
 constexpr int SK_NBUF = 4;  // TMEM accumulator buffers (segments in flight)
 constexpr uint32_t SK_TMEM_COLS = SK_NBUF * SK_TPU * SK_MN;
 constexpr int SK_SLOT = SK_TPU * SK_MN * SK_BN;  // floats per partial slot
-constexpr int SK_SMEM = SK_STAGES * SK_STAGE_BYTES + 512 + 1024;
+constexpr int SK_EPI_BYTES = SK_TPU * SK_MN * SK_BN * 4;  // finished block, fp32
+constexpr int SK_SMEM = SK_STAGES * SK_STAGE_BYTES + SK_EPI_BYTES + 512 + 1024;
+static_assert(SK_TPU * SK_BN == 256, "the finish maps 32 threads x 8 columns onto one row of a group");
 static_assert(SK_STAGE_BYTES % 1024 == 0, "stage alignment");
 static_assert(SK_TMEM_COLS >= 32 && (SK_TMEM_COLS & (SK_TMEM_COLS - 1)) == 0, "TMEM alloc size");
 
@@ -81,7 +83,8 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SK_STAGES * SK_STAGE_BYTES);
+  const uint32_t epi_u32 = smem_u32(smem + SK_STAGES * SK_STAGE_BYTES);  // finished block
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SK_STAGES * SK_STAGE_BYTES + SK_EPI_BYTES);
   constexpr int NB = 2 * SK_STAGES + 2 * SK_NBUF + 1;  // full, empty, tfull, tempty, done
   volatile int* s_abort = reinterpret_cast<volatile int*>(bars + NB);
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + NB + 1);
@@ -220,137 +223,162 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     int g = g_begin, kb = kb_begin, left = n_units;
-    while (left > 0) {
-      const int seg_units = min(left, p.KB - kb);
-      const bool whole_from_start = (kb == 0);
-      left -= seg_units;
-      // A row bias is loaded before the accumulator is ready, off the tail.
-      float bias_pre[SK_TPU];
-#pragma unroll
-      for (int j = 0; j < SK_TPU; ++j) {
-        const int n = (g * SK_TPU + j) * SK_BN + q * 32 + lane;
-        bias_pre[j] = (ep.operand_kind == OJX_OPERAND_ROW && n < p.N)
-                          ? load_elem(ep.operand, n, ep.dtype_operand)
-                          : 0.0f;
-      }
-      // The four epilogue warps meet at named barriers below, so they must agree
-      // on whether to go on: any warp that failed its wait stops all four.
-      const bool waited = mbar_wait(tfull_bar(acc), acc_phase, p.budget, s_abort);
-      if (named_bar_red_or(1, 128, !waited)) break;
-      tc_fence_after();
-      uint32_t r[SK_TPU][16];
-      const uint32_t tq = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
-                          static_cast<uint32_t>(acc * SK_TPU * SK_MN);
-#pragma unroll
-      for (int j = 0; j < SK_TPU; ++j) tmem_ld16(tq + j * SK_MN, r[j]);
-      tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(tempty_bar(acc));
-      if (++acc == SK_NBUF) {
-        acc = 0;
-        acc_phase ^= 1u;
-      }
+    // Pass 0 runs the finishing code once on zeros with its stores disabled, while
+    // the accumulators are still far from ready: the tail's first real finish then
+    // finds that code in the instruction caches instead of fetching it from memory
+    // behind the last contributor's reduction.  `warm` goes through an empty asm so
+    // the compiler cannot specialise (and duplicate) the loop body for pass 0.
+    int warm = 1;
+    while (true) {
+      asm volatile("" : "+r"(warm));
+      if (!warm && left <= 0) break;
       float v[SK_TPU][SK_MN];
-#pragma unroll
-      for (int j = 0; j < SK_TPU; ++j)
-#pragma unroll
-        for (int m = 0; m < SK_MN; ++m) v[j][m] = __uint_as_float(r[j][m]);
-
       bool finish = true;
-      const bool whole = whole_from_start && seg_units == p.KB;
-      if (!whole) {
-        const int c_first = cta_of_unit(static_cast<long long>(g) * p.KB, p);
-        const int c_last = cta_of_unit(min(static_cast<long long>(g + 1) * p.KB, p.U) - 1, p);
-        const int ncontrib = c_last - c_first + 1;
-        const int jc = blockIdx.x - c_first;
-        float* slot = p.partials + (static_cast<long long>(g) * p.maxc + jc) * SK_SLOT +
-                      q * 32 + lane;
+      // In the finish below, thread etid owns the 8 columns fc .. fc+7 of the
+      // group (fc = 8 * (etid % 32)) in rows etid / 32, + 4, + 8, + 12.  Their
+      // row operand (bias) is loaded here, before the accumulator is ready, so
+      // its latency is off the tail.
+      const int fc = 8 * (etid & 31);
+      const int fn = g * (SK_TPU * SK_BN) + fc;
+      const int fvalid = min(8, p.N - fn);
+      float row_op[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) row_op[k] = 0.0f;
+      if (ep.operand_kind == OJX_OPERAND_ROW && fvalid > 0)
+        load8(ep.operand, ep.dtype_operand, fn, fvalid, row_op);
+      if (warm) {
+#pragma unroll
+        for (int j = 0; j < SK_TPU; ++j)
+#pragma unroll
+          for (int m = 0; m < SK_MN; ++m) v[j][m] = 0.0f;
+      } else {
+        const int seg_units = min(left, p.KB - kb);
+        const bool whole_from_start = (kb == 0);
+        left -= seg_units;
+        // The four epilogue warps meet at named barriers below, so they must agree
+        // on whether to go on: any warp that failed its wait stops all four.
+        const bool waited = mbar_wait(tfull_bar(acc), acc_phase, p.budget, s_abort);
+        if (named_bar_red_or(1, 128, !waited)) break;
+        tc_fence_after();
+        uint32_t r[SK_TPU][16];
+        const uint32_t tq = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                            static_cast<uint32_t>(acc * SK_TPU * SK_MN);
+#pragma unroll
+        for (int j = 0; j < SK_TPU; ++j) tmem_ld16(tq + j * SK_MN, r[j]);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(tempty_bar(acc));
+        if (++acc == SK_NBUF) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+#pragma unroll
+        for (int j = 0; j < SK_TPU; ++j)
+#pragma unroll
+          for (int m = 0; m < SK_MN; ++m) v[j][m] = __uint_as_float(r[j][m]);
+        const bool whole = whole_from_start && seg_units == p.KB;
+        if (!whole) {
+          const int c_first = cta_of_unit(static_cast<long long>(g) * p.KB, p);
+          const int c_last = cta_of_unit(min(static_cast<long long>(g + 1) * p.KB, p.U) - 1, p);
+          const int ncontrib = c_last - c_first + 1;
+          const int jc = blockIdx.x - c_first;
+          float* slot = p.partials + (static_cast<long long>(g) * p.maxc + jc) * SK_SLOT +
+                        q * 32 + lane;
+#pragma unroll
+          for (int j = 0; j < SK_TPU; ++j)
+#pragma unroll
+            for (int m = 0; m < SK_MN; ++m)
+              if (m < p.M) slot[(j * SK_MN + m) * SK_BN] = v[j][m];
+          named_bar_sync(1, 128);
+          if (etid == 0) {
+            __threadfence();
+            unsigned long long* ctr = p.counters + g;
+            unsigned long long old = *reinterpret_cast<volatile unsigned long long*>(ctr);
+            unsigned int count;
+            while (true) {  // ends as soon as the CAS succeeds
+              const unsigned int e = static_cast<unsigned int>(old >> 32);
+              count = (e == p.epoch) ? static_cast<unsigned int>(old & 0xffffffffu) + 1u : 1u;
+              const unsigned long long nv = (static_cast<unsigned long long>(p.epoch) << 32) | count;
+              const unsigned long long seen = atomicCAS(ctr, old, nv);
+              if (seen == old) break;
+              old = seen;
+            }
+            *s_last = (count == static_cast<unsigned int>(ncontrib)) ? 1 : 0;
+            if (*s_last) {
+              *ctr = 0ull;  // every contributor of this group has arrived
+              __threadfence();
+            }
+          }
+          named_bar_sync(1, 128);
+          finish = *s_last != 0;
+          if (finish) {
+            // Sum the partials in contributor order; every load is issued before
+            // the first add of a contributor's slot.
+            const float* base = p.partials + static_cast<long long>(g) * p.maxc * SK_SLOT + q * 32 + lane;
+#pragma unroll
+            for (int j = 0; j < SK_TPU; ++j)
+#pragma unroll
+              for (int m = 0; m < SK_MN; ++m) v[j][m] = 0.0f;
+            for (int jj = 0; jj < ncontrib; ++jj) {
+              const float* sl = base + static_cast<long long>(jj) * SK_SLOT;
+              float t[SK_TPU][SK_MN];
+#pragma unroll
+              for (int j = 0; j < SK_TPU; ++j)
+#pragma unroll
+                for (int m = 0; m < SK_MN; ++m)
+                  t[j][m] = m < p.M ? __ldcg(sl + (j * SK_MN + m) * SK_BN) : 0.0f;
+#pragma unroll
+              for (int j = 0; j < SK_TPU; ++j)
+#pragma unroll
+                for (int m = 0; m < SK_MN; ++m) v[j][m] += t[j][m];
+            }
+          }
+          named_bar_sync(1, 128);  // s_last may be rewritten by the next segment
+        }
+      }
+      if (finish) {
+        // Stage the finished M x 256 block in shared memory, then each thread
+        // runs the 8-wide epilogue on its 8 columns of every fourth row and
+        // writes them with one 16-byte store per destination (a warp covers a
+        // whole 256-column row: 512 contiguous bytes).
 #pragma unroll
         for (int j = 0; j < SK_TPU; ++j)
 #pragma unroll
           for (int m = 0; m < SK_MN; ++m)
-            if (m < p.M) slot[(j * SK_MN + m) * SK_BN] = v[j][m];
+            if (m < p.M) st_shared_f32(epi_u32 + 4u * ((j * SK_MN + m) * SK_BN + q * 32 + lane), v[j][m]);
         named_bar_sync(1, 128);
-        if (etid == 0) {
-          __threadfence();
-          unsigned long long* ctr = p.counters + g;
-          unsigned long long old = *reinterpret_cast<volatile unsigned long long*>(ctr);
-          unsigned int count;
-          while (true) {  // ends as soon as the CAS succeeds
-            const unsigned int e = static_cast<unsigned int>(old >> 32);
-            count = (e == p.epoch) ? static_cast<unsigned int>(old & 0xffffffffu) + 1u : 1u;
-            const unsigned long long nv = (static_cast<unsigned long long>(p.epoch) << 32) | count;
-            const unsigned long long seen = atomicCAS(ctr, old, nv);
-            if (seen == old) break;
-            old = seen;
-          }
-          *s_last = (count == static_cast<unsigned int>(ncontrib)) ? 1 : 0;
-          if (*s_last) {
-            *ctr = 0ull;  // every contributor of this group has arrived
-            __threadfence();
-          }
-        }
-        named_bar_sync(1, 128);
-        finish = *s_last != 0;
-        if (finish) {
-          // Sum the partials in contributor order; every load is issued before
-          // the first add of a contributor's slot.
-          const float* base = p.partials + static_cast<long long>(g) * p.maxc * SK_SLOT + q * 32 + lane;
+        if (fvalid > 0) {
+#pragma unroll 1
+          for (int m = etid >> 5; m < p.M; m += 4) {
+            float y[8], x[8];
+            const uint32_t sa = epi_u32 + 4u * (((fc >> 7) * SK_MN + m) * SK_BN + (fc & 127));
 #pragma unroll
-          for (int j = 0; j < SK_TPU; ++j)
+            for (int k = 0; k < 8; ++k) y[k] = ld_shared_f32(sa + 4u * k);
+            if (ep.operand_kind == OJX_OPERAND_FULL)
+              load8(ep.operand, ep.dtype_operand, static_cast<int64_t>(m) * ep.ld_operand + fn,
+                    fvalid, x);
+            else
 #pragma unroll
-            for (int m = 0; m < SK_MN; ++m) v[j][m] = 0.0f;
-          for (int jj = 0; jj < ncontrib; ++jj) {
-            const float* sl = base + static_cast<long long>(jj) * SK_SLOT;
-            float t[SK_TPU][SK_MN];
+              for (int k = 0; k < 8; ++k) x[k] = row_op[k];
+            if (ep.operand_kind != OJX_OPERAND_NONE)
+              binary_n<8>(ep.binary_op, ep.operand_is_lhs != 0, y, x);
+            for (int i = 0; i < ep.n_unary; ++i) unary_n_half<8>(unary_at(ep.unary_packed, i), y);
+            if (!warm) {
 #pragma unroll
-            for (int j = 0; j < SK_TPU; ++j)
-#pragma unroll
-              for (int m = 0; m < SK_MN; ++m)
-                t[j][m] = m < p.M ? __ldcg(sl + (j * SK_MN + m) * SK_BN) : 0.0f;
-#pragma unroll
-            for (int j = 0; j < SK_TPU; ++j)
-#pragma unroll
-              for (int m = 0; m < SK_MN; ++m) v[j][m] += t[j][m];
-          }
-        }
-        named_bar_sync(1, 128);  // s_last may be rewritten by the next segment
-      }
-      if (finish) {
-#pragma unroll
-        for (int j = 0; j < SK_TPU; ++j) {
-          const int n = (g * SK_TPU + j) * SK_BN + q * 32 + lane;
-          if (n < p.N) {
-            // All operand loads first, then the op chain 16-wide, then the stores:
-            // interleaving them would serialise every load behind the previous
-            // store (C may alias the operand as far as the compiler knows).
-            if (ep.operand_kind != OJX_OPERAND_NONE) {
-              float x[SK_MN];
-              if (ep.operand_kind == OJX_OPERAND_ROW) {
-#pragma unroll
-                for (int m = 0; m < SK_MN; ++m) x[m] = bias_pre[j];
-              } else {
-#pragma unroll
-                for (int m = 0; m < SK_MN; ++m)
-                  x[m] = m < p.M ? load_elem(ep.operand, static_cast<int64_t>(m) * ep.ld_operand + n,
-                                             ep.dtype_operand)
-                                 : 0.0f;
+              for (int di = 0; di < OJX_MAX_PEERS; ++di) {
+                if (di >= ep.n_dst) break;
+                store8(ep.dst[di], ep.dtype_c, static_cast<int64_t>(m) * ep.ldc + ep.col_offset + fn,
+                       fvalid, y);
               }
-              binary16(ep.binary_op, ep.operand_is_lhs != 0, v[j], x);
-            }
-            for (int i = 0; i < ep.n_unary; ++i) unary16(unary_at(ep.unary_packed, i), v[j]);
-#pragma unroll
-            for (int di = 0; di < OJX_MAX_PEERS; ++di) {
-              if (di >= ep.n_dst) break;
-#pragma unroll
-              for (int m = 0; m < SK_MN; ++m)
-                if (m < p.M)
-                  store_elem(ep.dst[di], static_cast<int64_t>(m) * ep.ldc + ep.col_offset + n,
-                             ep.dtype_c, v[j][m]);
             }
           }
         }
+        named_bar_sync(1, 128);  // the staging block is rewritten by the next finish
+      }
+      if (warm) {
+        warm = 0;
+        continue;
       }
       kb = 0;
       ++g;
