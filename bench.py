@@ -424,6 +424,113 @@ def e2e_measure(args, lib, L, A, C, M, K, N, es, gemm, gather, world, dev, strea
             "note": "C-ABI with pinned host buffers; CUDA events on the launching stream, max over ranks"}
 
 
+def run_train(args, cfg):
+    """One training step of a linear layer on one GPU, through the C-ABI with the
+    operands resident: forward Y = X @ W^T + b (W stored [N, K] like nn.Linear),
+    backward dX = dY @ W, dW = dY^T @ X (both read the stored operands transposed
+    through the GEMM descriptor) and db = dY.sum(0).  The reference's
+    LinearFunction (torchcl/autograd.py:355-412) does the same with two
+    materialised transposes.  value = 3 * 2*M*N*K / step time."""
+    import torch
+    from torchcl import _lib as L
+
+    lib = L.lib()
+    torch.cuda.set_device(0)
+    L.check(lib.ojx_init(0, ctypes.byref(L.DeviceInfo())), "ojx_init")
+    dev = torch.device("cuda", 0)
+    tdt = torch.bfloat16 if cfg["dtype"] == "bf16" else torch.float32
+    code = L.BF16 if tdt == torch.bfloat16 else L.F32
+    es = 2 if code == L.BF16 else 4
+    M, N, K = cfg["M"], cfg["N"], cfg["K"]
+    g = torch.Generator(device=dev).manual_seed(cfg["seed"])
+    X = torch.randn(M, K, device=dev, generator=g).to(tdt)
+    W = (torch.randn(N, K, device=dev, generator=g) * cfg["w_scale"]).to(tdt)
+    b = (torch.randn(N, device=dev, generator=g) * 0.1).to(tdt)
+    G = torch.randn(M, N, device=dev, generator=g).to(tdt)
+    Y, dX = torch.empty(M, N, device=dev, dtype=tdt), torch.empty(M, K, device=dev, dtype=tdt)
+    dW, db = torch.empty(N, K, device=dev, dtype=tdt), torch.empty(N, device=dev, dtype=tdt)
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+
+    def desc(m, n, k, a, bb, c, ta=0, tb=0, bias=None):
+        d = L.GemmDesc()
+        d.M, d.N, d.K = m, n, k
+        d.dtype_a = d.dtype_b = d.dtype_c = d.dtype_operand = code
+        d.trans_a, d.trans_b = ta, tb
+        d.a, d.b, d.c = a.data_ptr(), bb.data_ptr(), c.data_ptr()
+        if bias is not None:
+            d.operand, d.operand_kind, d.binary_op = bias.data_ptr(), L.OPERAND_ROW, L.BINARY["add"]
+        return d
+
+    descs = [desc(M, N, K, X, W, Y, tb=1, bias=b),   # forward
+             desc(M, K, N, G, W, dX),                # dX = dY @ W
+             desc(N, K, M, G, X, dW, ta=1)]          # dW = dY^T @ X
+    names = ["forward", "grad_input", "grad_weight", "grad_bias"]
+
+    def step(evs=None):
+        for i, d in enumerate(descs):
+            if evs:
+                evs[i].record(stream)
+            L.check(lib.ojx_gemm(ctypes.byref(d), sp), names[i])
+        if evs:
+            evs[3].record(stream)
+        L.check(lib.ojx_sum_columns(db.data_ptr(), code, G.data_ptr(), code, M, N, 0, sp), "sum_columns")
+        if evs:
+            evs[4].record(stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    routes = []
+    for d in descs:
+        L.check(lib.ojx_gemm(ctypes.byref(d), sp))
+        routes.append(L.ROUTES.get(lib.ojx_last_route()))
+    torch.cuda.synchronize(dev)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
+    launches0 = lib.ojx_kernel_launch_count()
+    with ClockSampler(0) as clk:
+        torch.cuda._sleep(int(1e6 + 2e5 * args.steps))
+        for i in range(args.steps):
+            step(evs[i])
+        torch.cuda.synchronize(dev)
+    launches = lib.ojx_kernel_launch_count() - launches0
+    L.check(lib.ojx_poll_device_error(), "device error")
+    part = [[e[j].elapsed_time(e[j + 1]) for e in evs] for j in range(4)]
+    total_ms = sum(e[0].elapsed_time(e[4]) for e in evs)
+    flops = 3 * 2.0 * M * N * K
+    value = flops * args.steps / (total_ms / 1e3) / 1e12
+    peaks, peak_kind = _peaks()
+    peak = peaks.get("bf16_tflops", 1590.0) / (6 if code == L.F32 else 1)
+    per = {}
+    for j, name in enumerate(names[:3]):
+        ms = statistics.mean(part[j])
+        per[name] = {"route": routes[j], "ms": ms, "tflops": 2.0 * M * N * K / (ms / 1e3) / 1e12}
+    cs_ms = statistics.mean(part[3])
+    cs_bytes = M * N * es + N * es
+    per["grad_bias"] = {"ms": cs_ms, "gbs": cs_bytes / (cs_ms / 1e3) / 1e9,
+                        "frac_hbm": cs_bytes / (cs_ms / 1e3) / 1e9 / peaks["hbm_gbs"]}
+    top = max(per["forward"]["tflops"], per["grad_input"]["tflops"], per["grad_weight"]["tflops"])
+    clocks = clk.summary()
+    line = {"metric": f"linear-layer training step TFLOP/s (fwd + bwd, {cfg['desc']})", "value": value,
+            "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": cfg["dtype"], "data": "synthetic (seeded torch.Generator on device)",
+            "config": {"workload": f"{args.config} train: Y = X W^T + b, dX = dY W, dW = dY^T X, db = sum(dY)",
+                       "M": M, "N": N, "K": K,
+                       "l2": f"inputs larger than L2 (X {M * K * es / 1e6:.0f} MB, W {N * K * es / 1e6:.0f} MB, "
+                             f"dY {M * N * es / 1e6:.0f} MB); each GEMM streams two of them"},
+            "kernels": per,
+            "roofline": {"bound": "tensor", "achieved": flops / (sum(p["ms"] for k, p in per.items()
+                                                                     if k != "grad_bias") / 1e3) / 1e12,
+                         "peak": peak, "unit": "TFLOP/s", "best_gemm_tflops": top,
+                         "peak_source": f"{peak_kind} bf16_tflops{' / 6 (3xTF32)' if code == L.F32 else ''}"},
+            "gpu_launches": int(launches),
+            "clocks": {k: clocks[k] for k in ("sm_mhz", "sm_max_mhz", "reasons")}}
+    line["roofline"]["frac"] = line["roofline"]["achieved"] / peak
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def graph_measure(args, cfg, A, W, bias, dev, iters: int = 200):
     """Host dispatch vs graph replay of one step through the public torchcl API.
 
@@ -497,6 +604,8 @@ def main() -> int:
                     help="multi-GPU: all-gather fused into the GEMM epilogue (p2p) or NCCL")
     ap.add_argument("--m", type=int, default=None, help="override M (e.g. cfg4 M in {1,4,16})")
     ap.add_argument("--size", type=int, default=None, help="override M=N=K (cfg2 sweep)")
+    ap.add_argument("--train", action="store_true",
+                    help="one GPU: time a linear-layer training step (forward + backward GEMMs)")
     ap.add_argument("--graph", action="store_true",
                     help="one GPU: also time public-API dispatch vs graph replay of one step")
     args = ap.parse_args()
@@ -511,6 +620,8 @@ def main() -> int:
         world = int(os.environ.get("WORLD_SIZE", "1"))
         rank = int(os.environ.get("RANK", "0"))
         return run_reference(args, cfg, world, rank)
+    if args.train:
+        return run_train(args, cfg)
     world, rank, local = _dist_setup()
     if world > 1 and args.config != "cfg5" and args.config != "cfg4":
         if rank == 0:

@@ -214,6 +214,17 @@ int ojx_fill(void* out, double value, int64_t n, int32_t dtype, ojx_stream s);
  * precision.cl:7-27). */
 int ojx_cast(void* out, int32_t dtype_out, const void* in, int32_t dtype_in, int64_t n, ojx_stream s);
 
+/* out[c] = sum over r < rows of in[r * ld + c] (ld 0 = cols), accumulated in fp32:
+ * the bias gradient of a linear layer.  Replaces run_sum_columns
+ * (torchcl/ops/engine.py:807-822) and its kernel sum_columns_f32
+ * (torchcl/kernels/reduction.cl:170-181), called from LinearFunction.backward
+ * (torchcl/autograd.py:404-408).  The reference adds the rows of a column in
+ * order with one accumulator; here rows are summed in blocks of 64 (each block in
+ * row order, then the block sums in block order), which is deterministic and
+ * reads the input once at full bandwidth. */
+int ojx_sum_columns(void* out, int32_t dtype_out, const void* in, int32_t dtype_in, int64_t rows,
+                    int64_t cols, int64_t ld, ojx_stream s);
+
 /* ── multi-GPU: W column-sharded GEMM with the output all-gathered by the GEMM
  * epilogue itself.  The reference's only "distributed" code is a host-side loop
  * (torchcl/mesh/collective.py:33-91: to_cpu, torch.cat, to_opencl); there is no

@@ -66,6 +66,8 @@ int launch_transpose(void* out, const void* in, int64_t rows, int64_t cols, int 
                      cudaStream_t s);
 int launch_fill(void* out, double v, int64_t n, int dtype, cudaStream_t s);
 int launch_cast(void* out, int dt_out, const void* in, int dt_in, int64_t n, cudaStream_t s);
+int launch_sum_columns(void* out, int dt_out, const void* in, int dt_in, int64_t rows, int64_t cols,
+                       int64_t ld, cudaStream_t s);
 int read_and_clear_device_error(unsigned int* word);
 
 inline int dtype_size(int dt) { return dt == OJX_F32 ? 4 : 2; }

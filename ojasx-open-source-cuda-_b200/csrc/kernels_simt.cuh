@@ -203,6 +203,77 @@ int launch_cast(void* out, int dt_out, const void* in, int dt_in, int64_t n, cud
   return cuda_status(cudaGetLastError(), "cast launch");
 }
 
+// ── column sums (bias gradient) ─────────────────────────────────────────────
+// out[c] = sum over r of in[r * ld + c] in fp32.  Rows are split into blocks of
+// CS_ROWS: pass 1 gives every (block, column) pair one thread that sums its rows in
+// ascending order from 0 (8 loads in flight, added in row order), pass 2 adds the
+// block sums of a column in ascending block order.  The order is fixed, so the
+// result is deterministic; a warp reads 32 consecutive columns of a row per load.
+constexpr int CS_ROWS = 64;
+
+template <int DT>
+__device__ __forceinline__ float cs_load(const void* p, int64_t i) {
+  if (DT == OJX_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+  if (DT == OJX_F16) return __half2float(static_cast<const __half*>(p)[i]);
+  return static_cast<const float*>(p)[i];
+}
+
+template <int DT>
+__global__ void __launch_bounds__(256) colsum_block_kernel(const void* __restrict__ in, int64_t rows,
+                                                           int64_t cols, int64_t ld,
+                                                           float* __restrict__ part) {
+  const int64_t c = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (c >= cols) return;
+  const int64_t r0 = static_cast<int64_t>(blockIdx.y) * CS_ROWS;
+  const int64_t r1 = min(rows, r0 + CS_ROWS);
+  float s = 0.0f;
+  int64_t r = r0;
+  for (; r + 8 <= r1; r += 8) {
+    float x[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) x[k] = cs_load<DT>(in, (r + k) * ld + c);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) s = __fadd_rn(s, x[k]);
+  }
+  for (; r < r1; ++r) s = __fadd_rn(s, cs_load<DT>(in, r * ld + c));
+  part[static_cast<int64_t>(blockIdx.y) * cols + c] = s;
+}
+
+__global__ void __launch_bounds__(256) colsum_final_kernel(const float* __restrict__ part,
+                                                           int64_t n_blocks, int64_t cols,
+                                                           void* __restrict__ out, int dt_out) {
+  const int64_t c = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (c >= cols) return;
+  float s = 0.0f;
+  for (int64_t b = 0; b < n_blocks; ++b) s = __fadd_rn(s, part[b * cols + c]);
+  store_elem(out, c, dt_out, s);
+}
+
+int launch_sum_columns(void* out, int dt_out, const void* in, int dt_in, int64_t rows, int64_t cols,
+                       int64_t ld, cudaStream_t s) {
+  if (cols <= 0) return OJX_OK;
+  const int64_t n_blocks = (rows + CS_ROWS - 1) / CS_ROWS;
+  const dim3 grid_c(static_cast<unsigned>((cols + 255) / 256));
+  if (n_blocks == 0) return launch_fill(out, 0.0, cols, dt_out, s);
+  if (n_blocks > 65535 || grid_c.x > 2147483647u)
+    return set_error(OJX_ERR_INVALID, "ojx_sum_columns: %lld rows x %lld columns is too large",
+                     static_cast<long long>(rows), static_cast<long long>(cols));
+  float* part = static_cast<float*>(
+      stream_workspace(s, static_cast<size_t>(n_blocks * cols) * sizeof(float), 3, false));
+  if (!part) return workspace_error();
+  const dim3 grid1(grid_c.x, static_cast<unsigned>(n_blocks));
+  switch (dt_in) {
+    case OJX_BF16: colsum_block_kernel<OJX_BF16><<<grid1, 256, 0, s>>>(in, rows, cols, ld, part); break;
+    case OJX_F16: colsum_block_kernel<OJX_F16><<<grid1, 256, 0, s>>>(in, rows, cols, ld, part); break;
+    default: colsum_block_kernel<OJX_F32><<<grid1, 256, 0, s>>>(in, rows, cols, ld, part); break;
+  }
+  g_launches.fetch_add(1);
+  if (int st = cuda_status(cudaGetLastError(), "sum_columns launch")) return st;
+  colsum_final_kernel<<<grid_c, 256, 0, s>>>(part, n_blocks, cols, out, dt_out);
+  g_launches.fetch_add(1);
+  return cuda_status(cudaGetLastError(), "sum_columns launch");
+}
+
 int read_and_clear_device_error(unsigned int* word) {
   unsigned int zero = 0;
   int st = cuda_status(cudaMemcpyFromSymbol(word, g_dev_error, sizeof(unsigned int)),

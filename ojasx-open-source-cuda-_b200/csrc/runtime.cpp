@@ -585,6 +585,19 @@ int ojx_cast(void* out, int32_t dtype_out, const void* in, int32_t dtype_in, int
   return launch_cast(out, dtype_out, in, dtype_in, n, static_cast<cudaStream_t>(s));
 }
 
+int ojx_sum_columns(void* out, int32_t dtype_out, const void* in, int32_t dtype_in, int64_t rows,
+                    int64_t cols, int64_t ld, ojx_stream s) {
+  if (rows < 0 || cols < 0) return set_error(OJX_ERR_INVALID, "ojx_sum_columns: negative size");
+  if (cols == 0) return OJX_OK;
+  if (!out || (rows > 0 && !in)) return set_error(OJX_ERR_INVALID, "ojx_sum_columns: NULL pointer");
+  if (!valid_dtype(dtype_out) || !valid_dtype(dtype_in))
+    return set_error(OJX_ERR_INVALID, "ojx_sum_columns: unknown dtype");
+  if (ld == 0) ld = cols;
+  if (ld < cols) return set_error(OJX_ERR_INVALID, "ojx_sum_columns: ld %lld < cols %lld",
+                                  static_cast<long long>(ld), static_cast<long long>(cols));
+  return launch_sum_columns(out, dtype_out, in, dtype_in, rows, cols, ld, static_cast<cudaStream_t>(s));
+}
+
 int ojx_ipc_get_handle(void* dptr, void* handle_out) {
   if (!dptr || !handle_out) return set_error(OJX_ERR_INVALID, "ojx_ipc_get_handle: NULL pointer");
   static_assert(sizeof(cudaIpcMemHandle_t) == OJX_IPC_HANDLE_BYTES, "IPC handle size");

@@ -156,6 +156,14 @@ class OpenCLEngine:
         L.check(L.lib().ojx_cast(_addr(out_buf), ojx_dtype(dtype_out), _addr(in_buf),
                                  ojx_dtype(dtype_in), int(n), get_queue()), "cast")
 
+    def run_sum_columns(self, input_buf, out_buf, rows: int, cols: int, dtype_in=None,
+                        dtype_out=None) -> None:
+        """out[cols] = input[rows, cols].sum(0) in fp32 (engine.py:807-822)."""
+        L.check(L.lib().ojx_sum_columns(
+            _addr(out_buf), ojx_dtype(dtype_out if dtype_out is not None else getattr(out_buf, "dtype", None)),
+            _addr(input_buf), ojx_dtype(dtype_in if dtype_in is not None else getattr(input_buf, "dtype", None)),
+            int(rows), int(cols), 0, get_queue()), "sum_columns")
+
     def run_elementwise(self, out_buf, a_buf, b_buf, binary, unary, n: int, dtype_out=None,
                         dtype_a=None, dtype_b=None) -> None:
         """out[i] = unary(...(a[i] op b[i])) — the JIT's fused elementwise kernel."""

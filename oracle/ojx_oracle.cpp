@@ -235,4 +235,30 @@ int oracle_cast(void* out, int dt_out, const void* in, int dt_in, int64_t n) {
   return 0;
 }
 
+// out[c] = sum of in[r * ld + c] over r, in fp32 (the bias gradient: column sums).
+// block == 0: reduction.cl:170-181 sum_columns_f32 exactly (one accumulator from
+// 0.0f, rows in ascending order).  block > 0: the order of the GPU kernel (rows in
+// blocks of `block`, each block summed in ascending order from 0.0f, then the
+// block sums added in ascending order from 0.0f).
+int oracle_sum_columns(float* out, const void* in, int dt_in, int64_t rows, int64_t cols,
+                       int64_t ld, int64_t block) {
+  for (int64_t c = 0; c < cols; ++c) {
+    if (block <= 0) {
+      float s = 0.0f;
+      for (int64_t r = 0; r < rows; ++r) s = s + load(in, r * ld + c, dt_in);
+      out[c] = s;
+      continue;
+    }
+    float total = 0.0f;
+    for (int64_t r0 = 0; r0 < rows; r0 += block) {
+      float s = 0.0f;
+      const int64_t r1 = r0 + block < rows ? r0 + block : rows;
+      for (int64_t r = r0; r < r1; ++r) s = s + load(in, r * ld + c, dt_in);
+      total = total + s;
+    }
+    out[c] = total;
+  }
+  return 0;
+}
+
 }  // extern "C"

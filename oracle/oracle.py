@@ -51,6 +51,7 @@ def lib() -> ctypes.CDLL:
                                           _p, _p, _i, _i, _i64, _i, _i, _p, _i, _i, _i, _p, _i64]
         _lib.oracle_elementwise.argtypes = [_p, _i, _p, _i, _p, _i, _i, _p, _i, _i64]
         _lib.oracle_cast.argtypes = [_p, _i, _p, _i, _i64]
+        _lib.oracle_sum_columns.argtypes = [_p, _p, _i, _i64, _i64, _i64, _i64]
     return _lib
 
 
@@ -136,6 +137,16 @@ def cast(x: np.ndarray, dtype_in: int, dtype_out: int) -> np.ndarray:
     return out
 
 
+def sum_columns(x: np.ndarray, dtype_in: int = F32, block: int = 0) -> np.ndarray:
+    """fp32 column sums of a [rows, cols] array (float32 values or 16-bit patterns).
+    block=0 is the reference kernel's order; block=64 the GPU kernel's."""
+    x = np.ascontiguousarray(x)
+    rows, cols = x.shape
+    out = np.zeros(cols, dtype=np.float32)
+    lib().oracle_sum_columns(_ptr(out), _ptr(x), dtype_in, rows, cols, cols, block)
+    return out
+
+
 def bf16_bits(x: np.ndarray) -> np.ndarray:
     """fp32 -> bf16 bit patterns (round to nearest even)."""
     return cast(np.asarray(x, dtype=np.float32), F32, BF16)
@@ -165,6 +176,7 @@ class RefKernels:
         L.ref_unary.argtypes = [ctypes.c_char_p, _p, _p, _i]
         L.ref_pack_fp32_to_fp16.argtypes = [_p, _p, _i]
         L.ref_unpack_fp16_to_fp32.argtypes = [_p, _p, _i]
+        L.ref_sum_columns_f32.argtypes = [_p, _p, _i, _i]
         del f32p
         self.L = L
 
@@ -186,6 +198,13 @@ class RefKernels:
             name = "ref_matmul_reg_tiled_bias_f32" if kernel == "reg_tiled" else "ref_matmul_bias_f32"
             getattr(self.L, name)(_ptr(A), _ptr(B), _ptr(bias), _ptr(C), M, N, K)
         return C
+
+    def sum_columns(self, X):
+        X = np.ascontiguousarray(X, dtype=np.float32)
+        rows, cols = X.shape
+        out = np.zeros(cols, dtype=np.float32)
+        self.L.ref_sum_columns_f32(_ptr(X), _ptr(out), rows, cols)
+        return out
 
     def linear(self, A, W, bias=None):
         A = np.ascontiguousarray(A, dtype=np.float32)

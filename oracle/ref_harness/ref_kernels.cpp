@@ -1,7 +1,7 @@
 // ref_kernels.cpp — builds the OjasX reference's own OpenCL C kernels
-// (torchcl/kernels/matmul.cl, activation.cl, elementwise.cl, precision.cl, read
-// from the reference tree at build time; the paths are passed as -D macros by
-// oracle/build_oracle.py) for the host through clshim.h, and launches each with the
+// (torchcl/kernels/matmul.cl, activation.cl, elementwise.cl, precision.cl and
+// reduction.cl, read from the reference tree at build time; the paths are passed
+// as -D macros by oracle/build_oracle.py) for the host through clshim.h, and launches each with the
 // NDRange geometry torchcl/ops/engine.py gives it.
 // TEST INFRASTRUCTURE ONLY: output goes to oracle/_ref/ and is used to pin the
 // oracle restatement (ojx_oracle.cpp); nothing of the reference is copied here.
@@ -20,6 +20,16 @@ namespace cl_elementwise {
 namespace cl_precision {
 #include REF_PRECISION_CL
 }
+// reduction.cl takes __local pointers as kernel arguments, which the shim's
+// per-thread-static __local cannot express; inside this namespace __local is
+// empty.  Only sum_columns_f32 (no local memory) is launched from here.
+#undef __local
+#define __local
+namespace cl_reduction {
+#include REF_REDUCTION_CL
+}
+#undef __local
+#define __local static thread_local
 
 namespace {
 size_t up(size_t n, size_t m) { return (n + m - 1) / m * m; }
@@ -110,6 +120,13 @@ int ref_unary(const char* name, const float* a, float* c, int n) {
   else if (!std::strcmp(name, "log")) run1(n, [&] { cl_elementwise::log_f32(a, c, n); });
   else if (!std::strcmp(name, "sqrt")) run1(n, [&] { cl_elementwise::sqrt_f32(a, c, n); });
   else return 1;
+  return 0;
+}
+// reduction.cl:170-181 sum_columns_f32 over cols rounded up to 256 work-items
+// (engine.py:807-822); the kernel uses no local memory, so the group size does
+// not change its result.
+int ref_sum_columns_f32(const float* in, float* out, int rows, int cols) {
+  run1(size_t(cols), [&] { cl_reduction::sum_columns_f32(in, out, rows, cols); });
   return 0;
 }
 // precision.cl

@@ -6,7 +6,7 @@ Run in the development container (the reference tree is not present on GPU boxes
 the fixtures it writes are committed).  Two sources of truth are used:
 
 1. The reference's OpenCL C kernels (torchcl/kernels/matmul.cl, activation.cl,
-   precision.cl), compiled for the host by oracle/build_oracle.py through
+   precision.cl, reduction.cl), compiled for the host by oracle/build_oracle.py through
    oracle/ref_harness/clshim.h and launched with torchcl/ops/engine.py's geometry.
 2. The reference's JIT code generator: torchcl.jit.compiler.JITCompiler is imported
    from the reference tree (with a stand-in `pyopencl` module, since pyopencl is not
@@ -90,6 +90,18 @@ def gemm_cases(R: dict) -> dict:
     return out
 
 
+def reduction_cases(R: dict) -> dict:
+    # reduction.cl:170-181 sum_columns_f32: the bias gradient of LinearFunction.backward
+    # (torchcl/autograd.py:404-408), on a ragged and a taller gradient.
+    out = {}
+    for seed, rows, cols in ((70, 257, 300), (71, 1024, 96)):
+        X = _torch_randn(seed, rows, cols)
+        out[f"sum_columns_{rows}x{cols}"] = dict(
+            X=X, **{f"S_{v}": r.sum_columns(X) for v, r in R.items()},
+            meta=np.array(["sum_columns", ""]))
+    return out
+
+
 def activation_cases(R: dict) -> dict:
     # tests/test_cuda_correctness_baseline.py:34-51 (seed 202, 10 000 randn)
     x = _torch_randn(202, 10000)
@@ -170,15 +182,19 @@ def jit_cases(ref_root: str) -> dict:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref-root", default=build_oracle.DEFAULT_REF_ROOT)
+    ap.add_argument("--only", default=None, help="write only the fixtures of one group "
+                    "(gemm, activation, reduction, jit)")
     args = ap.parse_args()
     build_oracle.build_oracle()
     if not build_oracle.build_ref(args.ref_root):
         raise SystemExit(f"reference tree not found at {args.ref_root}")
     R = {"nofma": RefKernels("nofma"), "fma": RefKernels("fma")}
+    groups = {"gemm": lambda: gemm_cases(R), "activation": lambda: activation_cases(R),
+              "reduction": lambda: reduction_cases(R), "jit": lambda: jit_cases(args.ref_root)}
     fixtures = {}
-    fixtures.update(gemm_cases(R))
-    fixtures.update(activation_cases(R))
-    fixtures.update(jit_cases(args.ref_root))
+    for name, make in groups.items():
+        if args.only in (None, name):
+            fixtures.update(make())
     for name, rec in fixtures.items():
         np.savez_compressed(OUT / f"{name}.npz", **rec)
     print(f"wrote {len(fixtures)} fixtures to {OUT}")

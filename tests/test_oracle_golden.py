@@ -61,6 +61,18 @@ def test_fp16_golden(golden_dir, oracle_lib):
     np.testing.assert_array_equal(out, rec["C16_nofma"])
 
 
+@pytest.mark.parametrize("name", ["sum_columns_257x300", "sum_columns_1024x96"])
+def test_sum_columns_golden_bit_exact(golden_dir, oracle_lib, name):
+    """reduction.cl:170-181: the oracle's column sums in the reference's order."""
+    rec = _load(golden_dir, name)
+    out = O.sum_columns(rec["X"])
+    np.testing.assert_array_equal(out.view(np.uint32), rec["S_nofma"].view(np.uint32))
+    np.testing.assert_array_equal(out.view(np.uint32), rec["S_fma"].view(np.uint32))
+    # the GPU kernel's blocked order stays within the fp32 bar of the reference's
+    blocked = O.sum_columns(rec["X"], block=64)
+    assert np.linalg.norm(blocked - out) <= 1e-6 * np.linalg.norm(out)
+
+
 def test_transpose_golden(golden_dir):
     rec = _load(golden_dir, "transpose_16x32")
     np.testing.assert_array_equal(rec["A"].T, rec["T_nofma"])
