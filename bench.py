@@ -531,6 +531,84 @@ def run_train(args, cfg):
     return 0
 
 
+def run_batched(args, cfg):
+    """`--batch B` on one GPU: B independent problems of the config's shape (A_b, W_b,
+    per-problem bias row, fused activation) in ONE ojx_gemm_batched launch per step,
+    the reference's blas.bmm path (torchcl/blas/__init__.py:123-150).
+    value = B * 2*M*N*K / step time."""
+    import torch
+    from torchcl import _lib as L
+
+    lib = L.lib()
+    torch.cuda.set_device(0)
+    L.check(lib.ojx_init(0, ctypes.byref(L.DeviceInfo())), "ojx_init")
+    dev = torch.device("cuda", 0)
+    tdt = torch.bfloat16 if cfg["dtype"] == "bf16" else torch.float32
+    code = L.BF16 if tdt == torch.bfloat16 else L.F32
+    es = 2 if code == L.BF16 else 4
+    Bn, M, N, K = args.batch, cfg["M"], cfg["N"], cfg["K"]
+    g = torch.Generator(device=dev).manual_seed(cfg["seed"])
+    A = torch.randn(Bn, M, K, device=dev, generator=g).to(tdt)
+    W = (torch.randn(Bn, K, N, device=dev, generator=g) * cfg["w_scale"]).to(tdt)
+    bias = (torch.randn(Bn, N, device=dev, generator=g) * cfg["b_scale"]).to(tdt)
+    C = torch.empty(Bn, M, N, device=dev, dtype=tdt)
+    in_bytes = (A.numel() + W.numel()) * es
+    flush = torch.empty(256 * 1024 * 1024 if in_bytes < L2_BYTES else 1, device=dev, dtype=torch.uint8)
+    d = L.GemmDesc()
+    d.M, d.N, d.K = M, N, K
+    d.dtype_a = d.dtype_b = d.dtype_c = d.dtype_operand = code
+    d.a, d.b, d.c, d.operand = A.data_ptr(), W.data_ptr(), C.data_ptr(), bias.data_ptr()
+    d.operand_kind, d.binary_op = L.OPERAND_ROW, L.BINARY["add"]
+    d.n_unary, d.unary[0] = 1, L.UNARY[cfg["act"]]
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+
+    def step():
+        L.check(lib.ojx_gemm_batched(ctypes.byref(d), Bn, M * K, K * N, M * N, N, sp), "gemm_batched")
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    route = L.ROUTES.get(lib.ojx_last_route())
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    launches0 = lib.ojx_kernel_launch_count()
+    with ClockSampler(0) as clk:
+        torch.cuda._sleep(int(1e6 + 2e5 * args.steps))
+        for e0, e1 in evs:
+            if in_bytes < L2_BYTES:
+                flush.zero_()
+            e0.record(stream)
+            step()
+            e1.record(stream)
+        torch.cuda.synchronize(dev)
+    launches = lib.ojx_kernel_launch_count() - launches0
+    L.check(lib.ojx_poll_device_error(), "device error")
+    ms = [e0.elapsed_time(e1) for e0, e1 in evs]
+    total_ms = sum(ms)
+    flops = Bn * 2.0 * M * N * K
+    value = flops * args.steps / (total_ms / 1e3) / 1e12
+    peaks, peak_kind = _peaks()
+    peak = peaks.get("bf16_tflops", 1590.0) / (6 if code == L.F32 else 1)
+    clocks = clk.summary()
+    line = {"metric": f"batched fused GEMM TFLOP/s ({Bn} x {cfg['desc']})", "value": value,
+            "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": cfg["dtype"], "data": "synthetic (seeded torch.Generator on device)",
+            "config": {"workload": f"{args.config} x batch {Bn}: C_b = {cfg['act']}(A_b @ W_b + bias_b)",
+                       "batch": Bn, "M": M, "N": N, "K": K,
+                       "l2": "inputs larger than L2" if in_bytes >= L2_BYTES
+                             else "L2 flushed (256 MiB write) between timed iterations"},
+            "route": route,
+            "roofline": {"bound": "tensor", "achieved": value, "peak": peak, "unit": "TFLOP/s",
+                         "frac": value / peak,
+                         "peak_source": f"{peak_kind} bf16_tflops{' / 6 (3xTF32)' if code == L.F32 else ''}"},
+            "gpu_launches": int(launches),
+            "clocks": {k: clocks[k] for k in ("sm_mhz", "sm_max_mhz", "reasons")}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def graph_measure(args, cfg, A, W, bias, dev, iters: int = 200):
     """Host dispatch vs graph replay of one step through the public torchcl API.
 
@@ -604,6 +682,8 @@ def main() -> int:
                     help="multi-GPU: all-gather fused into the GEMM epilogue (p2p) or NCCL")
     ap.add_argument("--m", type=int, default=None, help="override M (e.g. cfg4 M in {1,4,16})")
     ap.add_argument("--size", type=int, default=None, help="override M=N=K (cfg2 sweep)")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="one GPU: time this many problems of the config's shape in one batched GEMM")
     ap.add_argument("--train", action="store_true",
                     help="one GPU: time a linear-layer training step (forward + backward GEMMs)")
     ap.add_argument("--graph", action="store_true",
@@ -622,6 +702,8 @@ def main() -> int:
         return run_reference(args, cfg, world, rank)
     if args.train:
         return run_train(args, cfg)
+    if args.batch:
+        return run_batched(args, cfg)
     world, rank, local = _dist_setup()
     if world > 1 and args.config != "cfg5" and args.config != "cfg4":
         if rank == 0:

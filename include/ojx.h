@@ -258,6 +258,18 @@ int ojx_gemm_allgather(const ojx_gemm_desc* d, void* const* c_peers, int32_t n_p
  * the array up; make it before capturing a stream. */
 int ojx_gemm_skinny_noalloc(const ojx_gemm_desc* d, ojx_stream s);
 
+/* Batched GEMM: problem b < batch computes C_b = epilogue(op(A_b) @ op(B_b)) with
+ * A_b = a + b*stride_a, B_b = b + b*stride_b, C_b = c + b*stride_c and its epilogue
+ * operand at operand + b*stride_operand (strides in elements; a stride of 0 shares
+ * one A, B or operand across the batch; outputs may not overlap).  bf16/fp16 and
+ * 3xTF32 problems run as ONE tcgen05 launch whose tile scheduler walks every
+ * problem's tiles (rank-3 TMA maps); other shapes run one launch per problem.
+ * Replaces blas.bmm (torchcl/blas/__init__.py:123-150, kernel
+ * matmul_batched_strided_f32 in torchcl/kernels/winograd_gemm.cl:91-119) and the
+ * PrivateUse1 per-batch loop cl_bmm (torchcl/runtime/privateuse1.py:216-234). */
+int ojx_gemm_batched(const ojx_gemm_desc* d, int64_t batch, int64_t stride_a, int64_t stride_b,
+                     int64_t stride_c, int64_t stride_operand, ojx_stream s);
+
 /* ── graph capture and replay ──────────────────────────────────────────────
  * Replaces torchcl/jit/graph_runner.py: `capture_graph` (:70-86) records the
  * launches made inside a `with` block and `CapturedGraph.replay` (:58-62)

@@ -38,6 +38,16 @@ struct StoreMaps {
   CUtensorMap m[OJX_MAX_PEERS];
 };
 
+// Batched GEMM (kernel instances with BATCH = 1): `batch` independent problems.
+// A and B come from rank-3 tensor maps whose third coordinate is the batch index
+// (a_bc / b_bc = 0: one matrix shared by every problem); C and the epilogue
+// operand of problem b start stride_c / stride_op elements after problem b-1's.
+struct BatchParams {
+  int batch;
+  int a_bc, b_bc;
+  int64_t stride_c, stride_op;
+};
+
 template <int KIND, int BN, int STAGES, int STORE_TMA = 0>
 struct TcLayout {
   static constexpr int ELEM = KIND == 0 ? 2 : 4;
@@ -79,15 +89,23 @@ __device__ __forceinline__ uint64_t operand_desc(uint32_t base, int ks) {
   return make_sw128_desc(base + ks * 32, 16, 1024);
 }
 
-// Loads of one operand tile (rows = 128 for A, BN for B) at (mn0, k0).
-template <int MN, int BK, int ROWS>
+// Loads of one operand tile (rows = 128 for A, BN for B) at (mn0, k0) of matrix bc.
+template <int MN, int BK, int ROWS, int BATCH>
 __device__ __forceinline__ void load_operand(uint32_t dst, const CUtensorMap* map, uint32_t bar,
-                                             int mn0, int k0) {
+                                             int mn0, int k0, int bc) {
   if (MN) {
 #pragma unroll
-    for (int j = 0; j < ROWS / 64; ++j) tma_load_2d(dst + j * (BK * 128), map, bar, mn0 + 64 * j, k0);
+    for (int j = 0; j < ROWS / 64; ++j) {
+      if (BATCH)
+        tma_load_3d(dst + j * (BK * 128), map, bar, mn0 + 64 * j, k0, bc);
+      else
+        tma_load_2d(dst + j * (BK * 128), map, bar, mn0 + 64 * j, k0);
+    }
   } else {
-    tma_load_2d(dst, map, bar, k0, mn0);
+    if (BATCH)
+      tma_load_3d(dst, map, bar, k0, mn0, bc);
+    else
+      tma_load_2d(dst, map, bar, k0, mn0);
   }
 }
 
@@ -143,10 +161,10 @@ __device__ __forceinline__ void store_row16(const EpiParams& ep, const uint32_t 
 // one tensor store per destination.  ESZ = output element bytes (chunk = 128/ESZ
 // columns).  `tcol` is the chunk's first TMEM column, `col0` its first output
 // column (relative to the destination maps), `row0` the box's first row.
-template <int ESZ>
+template <int ESZ, int BATCH>
 __device__ __forceinline__ void epi_chunk_tma(const EpiParams& ep, const StoreMaps& maps,
                                               uint32_t tcol, int64_t row, int M, int col0, int N,
-                                              uint32_t stage, int lane, int row0) {
+                                              uint32_t stage, int lane, int row0, int bidx) {
   constexpr int V = 128 / ESZ;
   float v[V];
 #pragma unroll
@@ -202,19 +220,22 @@ __device__ __forceinline__ void epi_chunk_tma(const EpiParams& ep, const StoreMa
 #pragma unroll
     for (int d = 0; d < OJX_MAX_PEERS; ++d) {
       if (d >= ep.n_dst) break;
-      tma_store_2d(&maps.m[d], stage, col0, row0);
+      if (BATCH)
+        tma_store_3d(&maps.m[d], stage, col0, row0, bidx);
+      else
+        tma_store_2d(&maps.m[d], stage, col0, row0);
     }
     bulk_commit_group();
   }
 }
 
-template <int KIND, int FMT, int A_MN, int B_MN, int BN, int STAGES, int STORE_TMA>
+template <int KIND, int FMT, int A_MN, int B_MN, int BN, int STAGES, int STORE_TMA, int BATCH = 0>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmA2,
                    const __grid_constant__ CUtensorMap tmB2, const EpiParams ep,
                    const __grid_constant__ StoreMaps smaps, const int M, const int N, const int K,
-                   const uint64_t budget, const int silence_producer) {
+                   const uint64_t budget, const int silence_producer, const BatchParams bp) {
   using L = TcLayout<KIND, BN, STAGES, STORE_TMA>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -267,7 +288,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
   const int tiles_m = (M + TC_BM - 1) / TC_BM;
   const int tiles_n = (N + BN - 1) / BN;
-  const int num_tiles = tiles_m * tiles_n;
+  const int tiles_per = tiles_m * tiles_n;  // per problem of a batch
+  const int num_tiles = BATCH ? tiles_per * bp.batch : tiles_per;
   const int KB = (K + L::BK - 1) / L::BK;
 
   if (warp == 0) {
@@ -277,9 +299,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       uint32_t phase = 0, issued = 0, issued_parity = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int bidx = BATCH ? tile / tiles_per : 0;
         int mb, nb;
-        tile_coords(tile, tiles_m, tiles_n, mb, nb);
+        tile_coords(tile - bidx * tiles_per, tiles_m, tiles_n, mb, nb);
         const int m0 = mb * TC_BM, n0 = nb * BN;
+        const int abc = bp.a_bc ? bidx : 0, bbc = bp.b_bc ? bidx : 0;
         for (int kb = 0; kb < KB; ++kb) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1u, budget, s_abort)) {
             ok = false;
@@ -290,11 +314,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           const uint32_t sA = sbase + stage * L::STAGE_BYTES;
           const uint32_t sB = sA + L::A_BYTES;
           const int k0 = kb * L::BK;
-          load_operand<A_MN, L::BK, TC_BM>(sA, &tmA, fb, m0, k0);
-          load_operand<B_MN, L::BK, BN>(sB, &tmB, fb, n0, k0);
+          load_operand<A_MN, L::BK, TC_BM, BATCH>(sA, &tmA, fb, m0, k0, abc);
+          load_operand<B_MN, L::BK, BN, BATCH>(sB, &tmB, fb, n0, k0, bbc);
           if (KIND == 1) {
-            load_operand<A_MN, L::BK, TC_BM>(sB + L::B_BYTES, &tmA2, fb, m0, k0);
-            load_operand<B_MN, L::BK, BN>(sB + L::B_BYTES + L::A_BYTES, &tmB2, fb, n0, k0);
+            load_operand<A_MN, L::BK, TC_BM, BATCH>(sB + L::B_BYTES, &tmA2, fb, m0, k0, abc);
+            load_operand<B_MN, L::BK, BN, BATCH>(sB + L::B_BYTES + L::A_BYTES, &tmB2, fb, n0, k0,
+                                                 bbc);
           }
           issued |= 1u << stage;
           issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
@@ -367,8 +392,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       if (!mbar_wait(tfull_bar(acc), acc_phase, budget, s_abort)) break;
       tc_fence_after();
+      const int bidx = BATCH ? tile / tiles_per : 0;
       int mb, nb;
-      tile_coords(tile, tiles_m, tiles_n, mb, nb);
+      tile_coords(tile - bidx * tiles_per, tiles_m, tiles_n, mb, nb);
+      // Problem bidx of a batch: its C and epilogue operand (ep is a copy, so
+      // only the pointers of the fields the epilogue reads move).
+      EpiParams epb = ep;
+      if (BATCH) {
+        const int esz_c = ep.dtype_c == OJX_F32 ? 4 : 2;
+        const int esz_o = ep.dtype_operand == OJX_F32 ? 4 : 2;
+        epb.dst[0] = static_cast<char*>(ep.dst[0]) + bidx * bp.stride_c * esz_c;
+        if (ep.operand)
+          epb.operand = static_cast<const char*>(ep.operand) + bidx * bp.stride_op * esz_o;
+      }
       const int64_t row = static_cast<int64_t>(mb) * TC_BM + q * 32 + lane;
       const int n0 = nb * BN + half * (BN / 2);
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
@@ -380,13 +416,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll 1
           for (int c = 0; c < BN / 2; c += 32) {
             if (n0 + c >= N) break;
-            epi_chunk_tma<4>(ep, smaps, tbase + c, row, M, n0 + c, N, stage_box, lane, row0);
+            epi_chunk_tma<4, BATCH>(epb, smaps, tbase + c, row, M, n0 + c, N, stage_box, lane, row0,
+                                    bidx);
           }
         } else {
 #pragma unroll 1
           for (int c = 0; c < BN / 2; c += 64) {
             if (n0 + c >= N) break;
-            epi_chunk_tma<2>(ep, smaps, tbase + c, row, M, n0 + c, N, stage_box, lane, row0);
+            epi_chunk_tma<2, BATCH>(epb, smaps, tbase + c, row, M, n0 + c, N, stage_box, lane, row0,
+                                    bidx);
           }
         }
       } else {
@@ -399,8 +437,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           tmem_ld16(tbase + c + 16, r1);
           tmem_wait_ld();
           if (row < M) {
-            store_row16(ep, r0, row, col0, N);
-            if (col0 + 16 < N) store_row16(ep, r1, row, col0 + 16, N);
+            store_row16(epb, r0, row, col0, N);
+            if (col0 + 16 < N) store_row16(epb, r1, row, col0 + 16, N);
           }
         }
       }
@@ -429,6 +467,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 // fp32 -> (hi, lo) tf32 parts, K-major [R][Kp], zero for k >= K.
 // Element (r, k) of the logical operand is src[r*ld + k] (trans == 0) or
 // src[k*ld + r] (trans == 1).  tf32 rounding: cvt.rna (round to nearest, ties away).
+// blockIdx.z selects one matrix of a batch: src_bs / dst_bs elements apart.
 __device__ __forceinline__ float to_tf32(float x) {
   uint32_t r;
   asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
@@ -438,8 +477,12 @@ __device__ __forceinline__ float to_tf32(float x) {
 __global__ void __launch_bounds__(256) split_tf32_kernel(const float* __restrict__ src, int64_t ld,
                                                          int trans, int R, int K, int Kp,
                                                          float* __restrict__ hi,
-                                                         float* __restrict__ lo) {
+                                                         float* __restrict__ lo, int64_t src_bs,
+                                                         int64_t dst_bs) {
   __shared__ float tile[32][33];
+  src += blockIdx.z * src_bs;
+  hi += blockIdx.z * dst_bs;
+  lo += blockIdx.z * dst_bs;
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
   const int k0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
   if (!trans) {
@@ -500,20 +543,21 @@ EpiParams make_epi(const ojx_gemm_desc& d, const Dests* dests) {
   return ep;
 }
 
-template <int KIND, int FMT, int A_MN, int B_MN, int BN, int STAGES, int STORE_TMA>
+template <int KIND, int FMT, int A_MN, int B_MN, int BN, int STAGES, int STORE_TMA, int BATCH>
 static int run_tc(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& a2,
                   const CUtensorMap& b2, const EpiParams& ep, const StoreMaps& sm, int M, int N,
-                  int K, cudaStream_t s) {
+                  int K, const BatchParams& bp, cudaStream_t s) {
   using L = TcLayout<KIND, BN, STAGES, STORE_TMA>;
-  auto kern = tc_gemm_kernel<KIND, FMT, A_MN, B_MN, BN, STAGES, STORE_TMA>;
+  auto kern = tc_gemm_kernel<KIND, FMT, A_MN, B_MN, BN, STAGES, STORE_TMA, BATCH>;
   int st = ensure_smem_attr(reinterpret_cast<const void*>(kern), L::SMEM_BYTES);
   if (st) return st;
   const DeviceProps& p = current_props();
-  const long tiles = static_cast<long>((M + TC_BM - 1) / TC_BM) * ((N + BN - 1) / BN);
+  const long tiles = static_cast<long>((M + TC_BM - 1) / TC_BM) * ((N + BN - 1) / BN) *
+                     (BATCH ? bp.batch : 1);
   const int grid = static_cast<int>(std::min<long>(tiles, p.sm_count));
   const int silence = g_silence_producer_once.exchange(0);
   kern<<<grid, TC_THREADS, L::SMEM_BYTES, s>>>(a, b, a2, b2, ep, sm, M, N, K, g_wait_budget.load(),
-                                               silence);
+                                               silence, bp);
   g_launches.fetch_add(1);
   return cuda_status(cudaGetLastError(), "tc_gemm launch");
 }
@@ -522,17 +566,21 @@ static int run_tc(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap&
 // at ep.dst[i] + col_offset with row stride ldc.  Returns false (no error) when an
 // address or the stride is not 16-byte aligned; the register-store epilogue is
 // used then.
-static bool make_store_maps(const EpiParams& ep, int M, int N, StoreMaps* sm) {
+static bool make_store_maps(const EpiParams& ep, int M, int N, StoreMaps* sm,
+                            const BatchInfo* bi = nullptr) {
   const int esz = ep.dtype_c == OJX_F32 ? 4 : 2;
   if ((ep.ldc * esz) % 16 != 0 || (ep.col_offset * esz) % 16 != 0) return false;
+  if (bi && (bi->stride_c * esz) % 16 != 0) return false;
   const CUtensorMapDataType dt = ep.dtype_c == OJX_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                                  : ep.dtype_c == OJX_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                           : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   for (int i = 0; i < ep.n_dst; ++i) {
     const char* base = static_cast<const char*>(ep.dst[i]) + ep.col_offset * esz;
     if (reinterpret_cast<uintptr_t>(base) % 16 != 0) return false;
-    if (make_tmap_2d_sw128(&sm->m[i], dt, esz, base, N, M, ep.ldc * esz, 128 / esz, 32) != OJX_OK)
-      return false;
+    const int st = bi ? make_tmap_3d_sw128(&sm->m[i], dt, esz, base, N, M, bi->batch, ep.ldc * esz,
+                                           bi->stride_c * esz, 128 / esz, 32)
+                      : make_tmap_2d_sw128(&sm->m[i], dt, esz, base, N, M, ep.ldc * esz, 128 / esz, 32);
+    if (st != OJX_OK) return false;
   }
   return true;
 }
@@ -545,37 +593,66 @@ bool tc_gemm_supported(const ojx_gemm_desc& d) {
   return true;
 }
 
-int launch_tc_gemm(const ojx_gemm_desc& d, cudaStream_t s, const Dests* dests) {
+// Rank-2 map of one operand, or for a batch the rank-3 map over all its matrices
+// (one matrix when stride == 0: every problem reads the same one).
+static int operand_map(CUtensorMap* m, CUtensorMapDataType dt, int esz, const void* base,
+                       uint64_t inner, uint64_t outer, int64_t ld, const BatchInfo* bi,
+                       int64_t stride, uint32_t box_inner, uint32_t box_outer) {
+  if (!bi) return make_tmap_2d_sw128(m, dt, esz, base, inner, outer, ld * esz, box_inner, box_outer);
+  const uint64_t nb = stride ? static_cast<uint64_t>(bi->batch) : 1;
+  const uint64_t bs = stride ? static_cast<uint64_t>(stride) * esz
+                             : (outer * ld * esz + 15) / 16 * 16;  // never stepped over
+  return make_tmap_3d_sw128(m, dt, esz, base, inner, outer, nb, ld * esz, bs, box_inner, box_outer);
+}
+
+static BatchParams batch_params(const BatchInfo* bi, bool a_batched, bool b_batched) {
+  BatchParams bp{};
+  bp.batch = bi ? static_cast<int>(bi->batch) : 1;
+  bp.a_bc = bi && a_batched ? 1 : 0;
+  bp.b_bc = bi && b_batched ? 1 : 0;
+  bp.stride_c = bi ? bi->stride_c : 0;
+  bp.stride_op = bi ? bi->stride_op : 0;
+  return bp;
+}
+
+int launch_tc_gemm(const ojx_gemm_desc& d, cudaStream_t s, const Dests* dests, const BatchInfo* bi) {
   const int M = static_cast<int>(d.M), N = static_cast<int>(d.N), K = static_cast<int>(d.K);
   const CUtensorMapDataType tdt =
       d.dtype_a == OJX_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   const DeviceProps& p = current_props();
   // BN = 256 unless that leaves most SMs idle.
-  const long tiles256 = static_cast<long>((M + 127) / 128) * ((N + 255) / 256);
+  const long tiles256 =
+      static_cast<long>((M + 127) / 128) * ((N + 255) / 256) * (bi ? bi->batch : 1);
   const int BN = tiles256 >= p.sm_count ? 256 : 128;
   CUtensorMap ta, tb;
   int st;
   // A: K-major [M,K] (box 64k x 128m) or MN-major [K,M] (box 64m x 64k).
   if (!d.trans_a)
-    st = make_tmap_2d_sw128(&ta, tdt, 2, d.a, K, M, d.lda * 2, 64, 128);
+    st = operand_map(&ta, tdt, 2, d.a, K, M, d.lda, bi, bi ? bi->stride_a : 0, 64, 128);
   else
-    st = make_tmap_2d_sw128(&ta, tdt, 2, d.a, M, K, d.lda * 2, 64, 64);
+    st = operand_map(&ta, tdt, 2, d.a, M, K, d.lda, bi, bi ? bi->stride_a : 0, 64, 64);
   if (st) return st;
   // B: MN-major [K,N] (box 64n x 64k) or K-major [N,K] (box 64k x BN).
   if (!d.trans_b)
-    st = make_tmap_2d_sw128(&tb, tdt, 2, d.b, N, K, d.ldb * 2, 64, 64);
+    st = operand_map(&tb, tdt, 2, d.b, N, K, d.ldb, bi, bi ? bi->stride_b : 0, 64, 64);
   else
-    st = make_tmap_2d_sw128(&tb, tdt, 2, d.b, K, N, d.ldb * 2, 64, BN);
+    st = operand_map(&tb, tdt, 2, d.b, K, N, d.ldb, bi, bi ? bi->stride_b : 0, 64, BN);
   if (st) return st;
   const EpiParams ep = make_epi(d, dests);
   StoreMaps sm;
-  const bool tma_out = make_store_maps(ep, M, N, &sm);
-  const bool bf = d.dtype_a == OJX_BF16;
+  const bool tma_out = make_store_maps(ep, M, N, &sm, bi);
+  if (bi && !tma_out)
+    return set_error(OJX_ERR_UNSUPPORTED, "batched tcgen05 GEMM needs 16-byte aligned C rows and strides");
+  const BatchParams bp = batch_params(bi, bi && bi->stride_a, bi && bi->stride_b);
+  const int fmt = d.dtype_a == OJX_BF16 ? 1 : 0;
   const int am = d.trans_a ? 1 : 0, bm = d.trans_b ? 0 : 1;
-#define OJX_TC_CASE(FMTV, AMN, BMN, BNV)                                                  \
-  if ((bf ? 1 : 0) == FMTV && am == AMN && bm == BMN && BN == BNV)                         \
-    return tma_out ? run_tc<0, FMTV, AMN, BMN, BNV, BNV == 256 ? 4 : 6, 1>(ta, tb, ta, tb, ep, sm, M, N, K, s) \
-                   : run_tc<0, FMTV, AMN, BMN, BNV, BNV == 256 ? 4 : 6, 0>(ta, tb, ta, tb, ep, sm, M, N, K, s);
+#define OJX_TC_CASE(FMTV, AMN, BMN, BNV)                                                        \
+  if (fmt == FMTV && am == AMN && bm == BMN && BN == BNV) {                                      \
+    constexpr int STG = BNV == 256 ? 4 : 6;                                                      \
+    if (bi) return run_tc<0, FMTV, AMN, BMN, BNV, STG, 1, 1>(ta, tb, ta, tb, ep, sm, M, N, K, bp, s); \
+    return tma_out ? run_tc<0, FMTV, AMN, BMN, BNV, STG, 1, 0>(ta, tb, ta, tb, ep, sm, M, N, K, bp, s) \
+                   : run_tc<0, FMTV, AMN, BMN, BNV, STG, 0, 0>(ta, tb, ta, tb, ep, sm, M, N, K, bp, s); \
+  }
 #define OJX_TC_BN(FMTV, AMN, BMN) \
   OJX_TC_CASE(FMTV, AMN, BMN, 256) OJX_TC_CASE(FMTV, AMN, BMN, 128)
   OJX_TC_BN(1, 0, 1) OJX_TC_BN(1, 0, 0) OJX_TC_BN(1, 1, 1) OJX_TC_BN(1, 1, 0)
@@ -585,40 +662,56 @@ int launch_tc_gemm(const ojx_gemm_desc& d, cudaStream_t s, const Dests* dests) {
   return set_error(OJX_ERR_UNSUPPORTED, "no tcgen05 GEMM instance for this layout");
 }
 
-int launch_tc_gemm_3xtf32(const ojx_gemm_desc& d, cudaStream_t s) {
+int launch_tc_gemm_3xtf32(const ojx_gemm_desc& d, cudaStream_t s, const BatchInfo* bi) {
   const int M = static_cast<int>(d.M), N = static_cast<int>(d.N), K = static_cast<int>(d.K);
   const int Kp = (K + 3) / 4 * 4;  // 16-byte row stride for TMA
+  // distinct A / B matrices of a batch (1 when one matrix is shared)
+  const int64_t nA = bi && bi->stride_a ? bi->batch : 1;
+  const int64_t nB = bi && bi->stride_b ? bi->batch : 1;
   auto al = [](size_t x) { return (x + 255) / 256 * 256; };
-  const size_t a_part = al(static_cast<size_t>(M) * Kp * 4);
-  const size_t b_part = al(static_cast<size_t>(N) * Kp * 4);
+  const size_t a_part = al(static_cast<size_t>(M) * Kp * 4 * nA);
+  const size_t b_part = al(static_cast<size_t>(N) * Kp * 4 * nB);
   char* ws = static_cast<char*>(stream_workspace(s, 2 * a_part + 2 * b_part, 0, false));
   if (!ws) return workspace_error();
   float* a_hi = reinterpret_cast<float*>(ws);
   float* a_lo = reinterpret_cast<float*>(ws + a_part);
   float* b_hi = reinterpret_cast<float*>(ws + 2 * a_part);
   float* b_lo = reinterpret_cast<float*>(ws + 2 * a_part + b_part);
-  // A -> [M][Kp]; op(B)^T -> [N][Kp] (the MMA's B operand is N x K, K-major).
+  // A -> [nA][M][Kp]; op(B)^T -> [nB][N][Kp] (the MMA's B operand is N x K, K-major).
   dim3 blk(256);
-  split_tf32_kernel<<<dim3((Kp + 31) / 32, (M + 31) / 32), blk, 0, s>>>(
-      static_cast<const float*>(d.a), d.lda, d.trans_a ? 1 : 0, M, K, Kp, a_hi, a_lo);
+  split_tf32_kernel<<<dim3((Kp + 31) / 32, (M + 31) / 32, static_cast<unsigned>(nA)), blk, 0, s>>>(
+      static_cast<const float*>(d.a), d.lda, d.trans_a ? 1 : 0, M, K, Kp, a_hi, a_lo,
+      bi ? bi->stride_a : 0, static_cast<int64_t>(M) * Kp);
   g_launches.fetch_add(1);
-  split_tf32_kernel<<<dim3((Kp + 31) / 32, (N + 31) / 32), blk, 0, s>>>(
-      static_cast<const float*>(d.b), d.ldb, d.trans_b ? 0 : 1, N, K, Kp, b_hi, b_lo);
+  split_tf32_kernel<<<dim3((Kp + 31) / 32, (N + 31) / 32, static_cast<unsigned>(nB)), blk, 0, s>>>(
+      static_cast<const float*>(d.b), d.ldb, d.trans_b ? 0 : 1, N, K, Kp, b_hi, b_lo,
+      bi ? bi->stride_b : 0, static_cast<int64_t>(N) * Kp);
   g_launches.fetch_add(1);
   int st = cuda_status(cudaGetLastError(), "split_tf32 launch");
   if (st) return st;
   constexpr int BN = 128;
   CUtensorMap ta, tb, ta2, tb2;
   const auto F = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
-  if ((st = make_tmap_2d_sw128(&ta, F, 4, a_hi, Kp, M, Kp * 4ull, 32, 128))) return st;
-  if ((st = make_tmap_2d_sw128(&ta2, F, 4, a_lo, Kp, M, Kp * 4ull, 32, 128))) return st;
-  if ((st = make_tmap_2d_sw128(&tb, F, 4, b_hi, Kp, N, Kp * 4ull, 32, BN))) return st;
-  if ((st = make_tmap_2d_sw128(&tb2, F, 4, b_lo, Kp, N, Kp * 4ull, 32, BN))) return st;
+  auto map = [&](CUtensorMap* m, const float* base, int rows, int64_t n, uint32_t box_rows) {
+    if (!bi) return make_tmap_2d_sw128(m, F, 4, base, Kp, rows, Kp * 4ull, 32, box_rows);
+    return make_tmap_3d_sw128(m, F, 4, base, Kp, rows, n, Kp * 4ull, static_cast<uint64_t>(rows) * Kp * 4,
+                              32, box_rows);
+  };
+  if ((st = map(&ta, a_hi, M, nA, 128))) return st;
+  if ((st = map(&ta2, a_lo, M, nA, 128))) return st;
+  if ((st = map(&tb, b_hi, N, nB, BN))) return st;
+  if ((st = map(&tb2, b_lo, N, nB, BN))) return st;
   const EpiParams ep = make_epi(d);
   StoreMaps sm;
-  if (make_store_maps(ep, M, N, &sm))
-    return run_tc<1, 2, 0, 0, BN, 3, 1>(ta, tb, ta2, tb2, ep, sm, M, N, Kp, s);
-  return run_tc<1, 2, 0, 0, BN, 3, 0>(ta, tb, ta2, tb2, ep, sm, M, N, Kp, s);
+  const bool tma_out = make_store_maps(ep, M, N, &sm, bi);
+  const BatchParams bp = batch_params(bi, nA > 1, nB > 1);
+  if (bi) {
+    if (!tma_out)
+      return set_error(OJX_ERR_UNSUPPORTED, "batched 3xTF32 GEMM needs 16-byte aligned C rows and strides");
+    return run_tc<1, 2, 0, 0, BN, 3, 1, 1>(ta, tb, ta2, tb2, ep, sm, M, N, Kp, bp, s);
+  }
+  if (tma_out) return run_tc<1, 2, 0, 0, BN, 3, 1, 0>(ta, tb, ta2, tb2, ep, sm, M, N, Kp, bp, s);
+  return run_tc<1, 2, 0, 0, BN, 3, 0, 0>(ta, tb, ta2, tb2, ep, sm, M, N, Kp, bp, s);
 }
 
 }  // namespace ojx

@@ -51,10 +51,19 @@ struct Dests {
   void* p[OJX_MAX_PEERS];
 };
 
+// A batch of GEMMs sharing one descriptor: problem b reads A at a + b*stride_a
+// elements (0: every problem reads the same A), likewise B, and writes C at
+// c + b*stride_c with its epilogue operand at operand + b*stride_op.
+struct BatchInfo {
+  int64_t batch;
+  int64_t stride_a, stride_b, stride_c, stride_op;
+};
+
 // Kernel families (implemented in the .cu files).  `dests` (optional) replaces
 // the single output d.c by several buffers written with the same values.
-int launch_tc_gemm(const ojx_gemm_desc& d, cudaStream_t s, const Dests* dests = nullptr);
-int launch_tc_gemm_3xtf32(const ojx_gemm_desc& d, cudaStream_t s);
+int launch_tc_gemm(const ojx_gemm_desc& d, cudaStream_t s, const Dests* dests = nullptr,
+                   const BatchInfo* bi = nullptr);
+int launch_tc_gemm_3xtf32(const ojx_gemm_desc& d, cudaStream_t s, const BatchInfo* bi = nullptr);
 int launch_skinny_gemm(const ojx_gemm_desc& d, cudaStream_t s, const Dests* dests = nullptr);
 int launch_simt_gemm(const ojx_gemm_desc& d, cudaStream_t s);
 bool tc_gemm_supported(const ojx_gemm_desc& d);

@@ -475,44 +475,52 @@ int ojx_event_elapsed_ms(ojx_event a, ojx_event b, float* ms) {
       "cudaEventElapsedTime");
 }
 
-int ojx_gemm(const ojx_gemm_desc* in, ojx_stream stream) {
-  set_last_route(OJX_ROUTE_NONE);
-  if (!in) return set_error(OJX_ERR_INVALID, "ojx_gemm: desc is NULL");
+}  // extern "C"
+
+namespace ojx {
+constexpr int kEmptyProblem = -1;
+
+// Checks a descriptor and fills in dense leading dimensions.  Returns OJX_OK,
+// kEmptyProblem (nothing to compute) or an error code.
+static int prepare_desc(const ojx_gemm_desc* in, ojx_gemm_desc* out, const char* who) {
+  if (!in) return set_error(OJX_ERR_INVALID, "%s: desc is NULL", who);
   ojx_gemm_desc d = *in;
   if (d.M < 0 || d.N < 0 || d.K < 0)
-    return set_error(OJX_ERR_INVALID, "ojx_gemm: negative dimension (%lld, %lld, %lld)",
+    return set_error(OJX_ERR_INVALID, "%s: negative dimension (%lld, %lld, %lld)", who,
                      (long long)d.M, (long long)d.N, (long long)d.K);
   if (!valid_dtype(d.dtype_a) || !valid_dtype(d.dtype_b) || !valid_dtype(d.dtype_c))
-    return set_error(OJX_ERR_INVALID, "ojx_gemm: unknown dtype");
+    return set_error(OJX_ERR_INVALID, "%s: unknown dtype", who);
   if (d.n_unary < 0 || d.n_unary > OJX_MAX_UNARY)
-    return set_error(OJX_ERR_INVALID, "ojx_gemm: n_unary %d out of range", d.n_unary);
+    return set_error(OJX_ERR_INVALID, "%s: n_unary %d out of range", who, d.n_unary);
   for (int i = 0; i < d.n_unary; ++i)
     if (!valid_unary(d.unary[i]))
-      return set_error(OJX_ERR_INVALID, "ojx_gemm: unknown unary op %d", d.unary[i]);
+      return set_error(OJX_ERR_INVALID, "%s: unknown unary op %d", who, d.unary[i]);
   if (d.operand_kind != OJX_OPERAND_NONE) {
     if (d.operand_kind != OJX_OPERAND_ROW && d.operand_kind != OJX_OPERAND_FULL)
-      return set_error(OJX_ERR_INVALID, "ojx_gemm: unknown operand kind %d", d.operand_kind);
-    if (!d.operand) return set_error(OJX_ERR_INVALID, "ojx_gemm: operand pointer is NULL");
+      return set_error(OJX_ERR_INVALID, "%s: unknown operand kind %d", who, d.operand_kind);
+    if (!d.operand) return set_error(OJX_ERR_INVALID, "%s: operand pointer is NULL", who);
     if (!valid_binary(d.binary_op))
-      return set_error(OJX_ERR_INVALID, "ojx_gemm: unknown binary op %d", d.binary_op);
+      return set_error(OJX_ERR_INVALID, "%s: unknown binary op %d", who, d.binary_op);
     if (!valid_dtype(d.dtype_operand))
-      return set_error(OJX_ERR_INVALID, "ojx_gemm: unknown operand dtype");
+      return set_error(OJX_ERR_INVALID, "%s: unknown operand dtype", who);
   }
-  if (d.M == 0 || d.N == 0) return OJX_OK;
+  if (d.M == 0 || d.N == 0) return kEmptyProblem;
   if (!d.c || (d.K > 0 && (!d.a || !d.b)))
-    return set_error(OJX_ERR_INVALID, "ojx_gemm: NULL matrix pointer");
+    return set_error(OJX_ERR_INVALID, "%s: NULL matrix pointer", who);
   if (d.lda == 0) d.lda = d.trans_a ? d.M : d.K;
   if (d.ldb == 0) d.ldb = d.trans_b ? d.K : d.N;
   if (d.ldc == 0) d.ldc = d.N;
   if (d.ld_operand == 0) d.ld_operand = d.N;
   if (d.lda < (d.trans_a ? d.M : d.K) || d.ldb < (d.trans_b ? d.K : d.N) || d.ldc < d.N ||
       (d.operand_kind == OJX_OPERAND_FULL && d.ld_operand < d.N))
-    return set_error(OJX_ERR_INVALID, "ojx_gemm: leading dimension smaller than the row length");
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const DeviceProps& p = current_props();
-  if (p.cc_major < 10)
-    return set_error(OJX_ERR_NOT_INITIALIZED, "ojx_gemm: current device is not sm_100 (call ojx_init)");
+    return set_error(OJX_ERR_INVALID, "%s: leading dimension smaller than the row length", who);
+  if (current_props().cc_major < 10)
+    return set_error(OJX_ERR_NOT_INITIALIZED, "%s: current device is not sm_100 (call ojx_init)", who);
+  *out = d;
+  return OJX_OK;
+}
 
+static int gemm_one(const ojx_gemm_desc& d, cudaStream_t s) {
   const bool f16 = d.dtype_a == d.dtype_b && (d.dtype_a == OJX_BF16 || d.dtype_a == OJX_F16);
   const bool f32 = d.dtype_a == OJX_F32 && d.dtype_b == OJX_F32;
   int route = OJX_ROUTE_SIMT;
@@ -537,6 +545,74 @@ int ojx_gemm(const ojx_gemm_desc* in, ojx_stream stream) {
   }
   if (st == OJX_OK) set_last_route(route);
   return st;
+}
+}  // namespace ojx
+
+extern "C" {
+
+int ojx_gemm(const ojx_gemm_desc* in, ojx_stream stream) {
+  set_last_route(OJX_ROUTE_NONE);
+  ojx_gemm_desc d;
+  const int st = prepare_desc(in, &d, "ojx_gemm");
+  if (st == kEmptyProblem) return OJX_OK;
+  if (st) return st;
+  return gemm_one(d, static_cast<cudaStream_t>(stream));
+}
+
+int ojx_gemm_batched(const ojx_gemm_desc* in, int64_t batch, int64_t stride_a, int64_t stride_b,
+                     int64_t stride_c, int64_t stride_operand, ojx_stream stream) {
+  set_last_route(OJX_ROUTE_NONE);
+  if (batch < 0 || stride_a < 0 || stride_b < 0 || stride_c < 0 || stride_operand < 0)
+    return set_error(OJX_ERR_INVALID, "ojx_gemm_batched: negative batch or stride");
+  if (batch == 0) return OJX_OK;
+  ojx_gemm_desc d;
+  int st = prepare_desc(in, &d, "ojx_gemm_batched");
+  if (st == kEmptyProblem) return OJX_OK;
+  if (st) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (batch == 1) return gemm_one(d, s);
+  if (stride_c < (d.M - 1) * d.ldc + d.N)
+    return set_error(OJX_ERR_INVALID,
+                     "ojx_gemm_batched: stride_c %lld makes the problems' outputs overlap",
+                     (long long)stride_c);
+  const bool f16 = d.dtype_a == d.dtype_b && (d.dtype_a == OJX_BF16 || d.dtype_a == OJX_F16);
+  const bool f32 = d.dtype_a == OJX_F32 && d.dtype_b == OJX_F32;
+  const int64_t tiles = ((d.M + 127) / 128) * ((d.N + 127) / 128) * batch;
+  const bool one_launch = !(d.flags & OJX_GEMM_FLAG_FORCE_SIMT) && d.K > 0 && tiles <= INT32_MAX &&
+                          batch <= 65535;
+  BatchInfo bi{batch, stride_a, stride_b, stride_c, stride_operand};
+  // The f16 kernel reads A and B through rank-3 TMA maps: their batch strides must
+  // be 16-byte multiples.  The 3xTF32 path copies its operands into its own
+  // aligned layout first, so any stride works there.
+  if (one_launch && f16 && tc_gemm_supported(d) && (stride_a * 2) % 16 == 0 &&
+      (stride_b * 2) % 16 == 0) {
+    st = launch_tc_gemm(d, s, nullptr, &bi);
+    if (st == OJX_OK) {
+      set_last_route(OJX_ROUTE_TC_F16);
+      return OJX_OK;
+    }
+    if (st != OJX_ERR_UNSUPPORTED) return st;
+  } else if (one_launch && f32 && d.fp32_mode != OJX_FP32_FFMA && d.M <= INT32_MAX &&
+             d.N <= INT32_MAX && d.K <= INT32_MAX && (d.fp32_mode == OJX_FP32_3XTF32 || d.M > 16)) {
+    st = launch_tc_gemm_3xtf32(d, s, &bi);
+    if (st == OJX_OK) {
+      set_last_route(OJX_ROUTE_TC_3XTF32);
+      return OJX_OK;
+    }
+    if (st != OJX_ERR_UNSUPPORTED) return st;
+  }
+  // Any other case: one launch per problem on the stream, in order.
+  const int ea = dtype_size(d.dtype_a), eb = dtype_size(d.dtype_b), ec = dtype_size(d.dtype_c);
+  const int eo = dtype_size(d.dtype_operand);
+  for (int64_t b = 0; b < batch; ++b) {
+    ojx_gemm_desc db = d;
+    db.a = static_cast<const char*>(d.a) + b * stride_a * ea;
+    db.b = static_cast<const char*>(d.b) + b * stride_b * eb;
+    db.c = static_cast<char*>(d.c) + b * stride_c * ec;
+    if (d.operand) db.operand = static_cast<const char*>(d.operand) + b * stride_operand * eo;
+    if ((st = gemm_one(db, s))) return st;
+  }
+  return OJX_OK;
 }
 
 int ojx_elementwise(void* out, int32_t dtype_out, const void* a, int32_t dtype_a, const void* b,

@@ -22,4 +22,11 @@ int make_tmap_2d_sw128_uncached(CUtensorMap* map, CUtensorMapDataType dtype, int
                                 const void* base, uint64_t inner, uint64_t outer,
                                 uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer);
 
+// 3-D: `batch` matrices of outer x inner, `batch_stride_bytes` apart (a multiple of
+// 16); the box covers one matrix (box_inner x box_outer x 1).
+int make_tmap_3d_sw128(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes,
+                       const void* base, uint64_t inner, uint64_t outer, uint64_t batch,
+                       uint64_t row_stride_bytes, uint64_t batch_stride_bytes,
+                       uint32_t box_inner, uint32_t box_outer);
+
 }  // namespace ojx

@@ -120,6 +120,8 @@ _SIGS = {
     "ojx_transpose": ([_P, _P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int32, _P], ctypes.c_int),
     "ojx_fill": ([_P, ctypes.c_double, ctypes.c_int64, ctypes.c_int32, _P], ctypes.c_int),
     "ojx_cast": ([_P, ctypes.c_int32, _P, ctypes.c_int32, ctypes.c_int64, _P], ctypes.c_int),
+    "ojx_gemm_batched": ([ctypes.POINTER(GemmDesc), ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                          ctypes.c_int64, ctypes.c_int64, _P], ctypes.c_int),
     "ojx_sum_columns": ([_P, ctypes.c_int32, _P, ctypes.c_int32, ctypes.c_int64, ctypes.c_int64,
                          ctypes.c_int64, _P], ctypes.c_int),
     "ojx_ipc_get_handle": ([_P, _P], ctypes.c_int),

@@ -32,30 +32,34 @@ def gemm(a, b, bias=None, activation: str | None = None, strategy: str | None = 
 
 
 def bmm(a, b):
-    """[B, M, K] @ [B, K, N] -> [B, M, N] (blas/__init__.py:123-150): one fused GEMM
-    launch per batch entry on slices of the device buffers."""
-    from torchcl.ops.engine import get_engine, ojx_dtype
+    """[B, M, K] @ [B, K, N] -> [B, M, N] (blas/__init__.py:123-150): ONE batched
+    GEMM launch (ojx_gemm_batched) whose tile scheduler walks all B problems; the
+    reference launches one naive work-item per output element
+    (winograd_gemm.cl:91-119).  A [M, K] or [K, N] second operand (2-D) is shared
+    by every batch entry."""
+    from torchcl.ops.engine import get_engine
     if not api.is_opencl_tensor(a):
         a = api.to_opencl(a)
     if not api.is_opencl_tensor(b):
         b = api.to_opencl(b)
     sa, sb = api._get_shape(a), api._get_shape(b)
-    if len(sa) != 3 or len(sb) != 3:
+    if len(sa) != 3 or len(sb) not in (2, 3):
         raise ValueError("bmm requires 3D tensors")
     B, M, K = sa
-    B2, K2, N = sb
+    if len(sb) == 3:
+        B2, K2, N = sb
+    else:
+        (K2, N), B2 = sb, B
     if B != B2 or K != K2:
         raise ValueError(f"Shape mismatch in bmm: {sa} vs {sb}")
     dt = api._get_dtype(a)
     if api._get_dtype(b) != dt:
         raise ValueError("bmm dtype mismatch")
-    es = 4 if ojx_dtype(dt) == 0 else 2
     engine = get_engine()
     abuf, bbuf = api._get_buf(a), api._get_buf(b)
     out = engine.allocate_output((B, M, N), dt)
-    for i in range(B):
-        engine.gemm(abuf.buffer + i * M * K * es, bbuf.buffer + i * K * N * es,
-                    out.buffer + i * M * N * es, M, N, K, dtype_a=dt, dtype_b=dt, dtype_c=dt)
+    engine.gemm(abuf, bbuf, out, M, N, K, dtype_a=dt, dtype_b=dt, dtype_c=dt, batch=B,
+                stride_a=M * K, stride_b=K * N if len(sb) == 3 else 0, stride_c=M * N)
     return api._wrap_output(out, (B, M, N), dt)
 
 

@@ -90,8 +90,10 @@ class OpenCLEngine:
     def gemm(self, a_buf, b_buf, out_buf, M: int, N: int, K: int, *, dtype_a=None, dtype_b=None,
              dtype_c=None, trans_a=False, trans_b=False, lda=0, ldb=0, ldc=0, operand=None,
              operand_kind=None, operand_dtype=None, ld_operand=0, binary="add",
-             operand_is_lhs=False, unary=(), fp32_mode=L.FP32_AUTO, flags=0, stream=None) -> str:
-        """One fused GEMM: out = unary(...(bin(op(A) @ op(B), operand)))."""
+             operand_is_lhs=False, unary=(), fp32_mode=L.FP32_AUTO, flags=0, stream=None,
+             batch=None, stride_a=0, stride_b=0, stride_c=0, stride_operand=0) -> str:
+        """One fused GEMM: out = unary(...(bin(op(A) @ op(B), operand))).  With `batch`,
+        `batch` problems whose operands are stride_* elements apart (ojx_gemm_batched)."""
         d = L.GemmDesc()
         d.M, d.N, d.K = int(M), int(N), int(K)
         d.dtype_a = ojx_dtype(dtype_a if dtype_a is not None else getattr(a_buf, "dtype", None))
@@ -120,7 +122,11 @@ class OpenCLEngine:
         d.flags = int(flags)
         q = get_queue() if stream is None else stream
         lib = L.lib()
-        L.check(lib.ojx_gemm(ctypes.byref(d), q), "gemm")
+        if batch is None:
+            L.check(lib.ojx_gemm(ctypes.byref(d), q), "gemm")
+        else:
+            L.check(lib.ojx_gemm_batched(ctypes.byref(d), int(batch), int(stride_a), int(stride_b),
+                                         int(stride_c), int(stride_operand), q), "gemm_batched")
         self.last_route = L.ROUTES.get(lib.ojx_last_route(), "?")
         return self.last_route
 

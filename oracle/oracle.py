@@ -177,6 +177,7 @@ class RefKernels:
         L.ref_pack_fp32_to_fp16.argtypes = [_p, _p, _i]
         L.ref_unpack_fp16_to_fp32.argtypes = [_p, _p, _i]
         L.ref_sum_columns_f32.argtypes = [_p, _p, _i, _i]
+        L.ref_matmul_batched_strided_f32.argtypes = [_p, _p, _p, _i, _i, _i, _i]
         del f32p
         self.L = L
 
@@ -197,6 +198,15 @@ class RefKernels:
             bias = np.ascontiguousarray(bias, dtype=np.float32)
             name = "ref_matmul_reg_tiled_bias_f32" if kernel == "reg_tiled" else "ref_matmul_bias_f32"
             getattr(self.L, name)(_ptr(A), _ptr(B), _ptr(bias), _ptr(C), M, N, K)
+        return C
+
+    def bmm(self, A, B):
+        A = np.ascontiguousarray(A, dtype=np.float32)
+        B = np.ascontiguousarray(B, dtype=np.float32)
+        batch, M, K = A.shape
+        N = B.shape[2]
+        C = np.zeros((batch, M, N), dtype=np.float32)
+        self.L.ref_matmul_batched_strided_f32(_ptr(A), _ptr(B), _ptr(C), batch, M, N, K)
         return C
 
     def sum_columns(self, X):

@@ -83,11 +83,16 @@ void barrier_yield() {
 }
 
 void run_ndrange(const size_t global[2], const size_t local[2], const std::function<void()>& call) {
-  if (global[0] % local[0] || global[1] % local[1])
+  const size_t g3[3] = {global[0], global[1], 1}, l3[3] = {local[0], local[1], 1};
+  run_ndrange3(g3, l3, call);
+}
+
+void run_ndrange3(const size_t global[3], const size_t local[3], const std::function<void()>& call) {
+  if (global[0] % local[0] || global[1] % local[1] || global[2] % local[2])
     throw std::runtime_error("global size must be a multiple of the local size");
-  const size_t ng0 = global[0] / local[0], ng1 = global[1] / local[1];
-  const size_t nwi = local[0] * local[1];
-  const long long ngroups = static_cast<long long>(ng0 * ng1);
+  const size_t ng0 = global[0] / local[0], ng1 = global[1] / local[1], ng2 = global[2] / local[2];
+  const size_t nwi = local[0] * local[1] * local[2];
+  const long long ngroups = static_cast<long long>(ng0 * ng1 * ng2);
 #pragma omp parallel
   {
     Group g;
@@ -97,17 +102,18 @@ void run_ndrange(const size_t global[2], const size_t local[2], const std::funct
     t_group = &g;
 #pragma omp for schedule(dynamic, 1)
     for (long long gi = 0; gi < ngroups; ++gi) {
-      const size_t gx = static_cast<size_t>(gi) % ng0, gy = static_cast<size_t>(gi) / ng0;
+      const size_t gx = static_cast<size_t>(gi) % ng0, gy = (static_cast<size_t>(gi) / ng0) % ng1;
+      const size_t gz = static_cast<size_t>(gi) / (ng0 * ng1);
       for (size_t i = 0; i < nwi; ++i) {
         Fiber& f = g.fibers[i];
-        const size_t lx = i % local[0], ly = i / local[0];
+        const size_t lx = i % local[0], ly = (i / local[0]) % local[1], lz = i / (local[0] * local[1]);
         f.done = false;
-        f.wi = WorkItem{{gx * local[0] + lx, gy * local[1] + ly, 0},
-                        {lx, ly, 0},
-                        {gx, gy, 0},
-                        {local[0], local[1], 1},
-                        {global[0], global[1], 1},
-                        {ng0, ng1, 1}};
+        f.wi = WorkItem{{gx * local[0] + lx, gy * local[1] + ly, gz * local[2] + lz},
+                        {lx, ly, lz},
+                        {gx, gy, gz},
+                        {local[0], local[1], local[2]},
+                        {global[0], global[1], global[2]},
+                        {ng0, ng1, ng2}};
         f.sp = init_stack(g.stacks.data() + i * kStack);
       }
       bool alive = true;

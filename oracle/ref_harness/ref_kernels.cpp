@@ -1,6 +1,6 @@
 // ref_kernels.cpp — builds the OjasX reference's own OpenCL C kernels
-// (torchcl/kernels/matmul.cl, activation.cl, elementwise.cl, precision.cl and
-// reduction.cl, read from the reference tree at build time; the paths are passed
+// (torchcl/kernels/matmul.cl, activation.cl, elementwise.cl, precision.cl,
+// reduction.cl and winograd_gemm.cl, read from the reference tree at build time; the paths are passed
 // as -D macros by oracle/build_oracle.py) for the host through clshim.h, and launches each with the
 // NDRange geometry torchcl/ops/engine.py gives it.
 // TEST INFRASTRUCTURE ONLY: output goes to oracle/_ref/ and is used to pin the
@@ -30,6 +30,9 @@ namespace cl_reduction {
 }
 #undef __local
 #define __local static thread_local
+namespace cl_winograd {
+#include REF_WINOGRAD_GEMM_CL
+}
 
 namespace {
 size_t up(size_t n, size_t m) { return (n + m - 1) / m * m; }
@@ -127,6 +130,16 @@ int ref_unary(const char* name, const float* a, float* c, int n) {
 // not change its result.
 int ref_sum_columns_f32(const float* in, float* out, int rows, int cols) {
   run1(size_t(cols), [&] { cl_reduction::sum_columns_f32(in, out, rows, cols); });
+  return 0;
+}
+// winograd_gemm.cl:91-119 matmul_batched_strided_f32 with blas.bmm's geometry
+// (global (N, M, B), local chosen by the runtime: one work-item per group here).
+int ref_matmul_batched_strided_f32(const float* A, const float* B, float* C, int batch, int M,
+                                   int N, int K) {
+  const size_t g[3] = {size_t(N), size_t(M), size_t(batch)}, l[3] = {1, 1, 1};
+  clshim::run_ndrange3(g, l, [&] {
+    cl_winograd::matmul_batched_strided_f32(A, B, C, batch, M, N, K, M * K, K * N, M * N);
+  });
   return 0;
 }
 // precision.cl

@@ -6,7 +6,7 @@ Run in the development container (the reference tree is not present on GPU boxes
 the fixtures it writes are committed).  Two sources of truth are used:
 
 1. The reference's OpenCL C kernels (torchcl/kernels/matmul.cl, activation.cl,
-   precision.cl, reduction.cl), compiled for the host by oracle/build_oracle.py through
+   precision.cl, reduction.cl, winograd_gemm.cl), compiled for the host by oracle/build_oracle.py through
    oracle/ref_harness/clshim.h and launched with torchcl/ops/engine.py's geometry.
 2. The reference's JIT code generator: torchcl.jit.compiler.JITCompiler is imported
    from the reference tree (with a stand-in `pyopencl` module, since pyopencl is not
@@ -88,6 +88,17 @@ def gemm_cases(R: dict) -> dict:
     X = _torch_randn(60, 16, 32)
     out["transpose_16x32"] = dict(A=X, T_nofma=R["nofma"].transpose(X), meta=np.array(["transpose", ""]))
     return out
+
+
+def batched_cases(R: dict) -> dict:
+    # tests/test_ojas_blas.py:55-66 (torch.manual_seed(42); A [4,32,64], B [4,64,32]) through
+    # winograd_gemm.cl:91-119 matmul_batched_strided_f32, as blas.bmm launches it.
+    import torch
+    torch.manual_seed(42)
+    A = torch.randn(4, 32, 64).numpy()
+    B = torch.randn(4, 64, 32).numpy()
+    return {"bmm_42": dict(A=A, B=B, **{f"C_{v}": r.bmm(A, B) for v, r in R.items()},
+                           meta=np.array(["bmm", ""]))}
 
 
 def reduction_cases(R: dict) -> dict:
@@ -183,14 +194,15 @@ def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref-root", default=build_oracle.DEFAULT_REF_ROOT)
     ap.add_argument("--only", default=None, help="write only the fixtures of one group "
-                    "(gemm, activation, reduction, jit)")
+                    "(gemm, activation, reduction, batched, jit)")
     args = ap.parse_args()
     build_oracle.build_oracle()
     if not build_oracle.build_ref(args.ref_root):
         raise SystemExit(f"reference tree not found at {args.ref_root}")
     R = {"nofma": RefKernels("nofma"), "fma": RefKernels("fma")}
     groups = {"gemm": lambda: gemm_cases(R), "activation": lambda: activation_cases(R),
-              "reduction": lambda: reduction_cases(R), "jit": lambda: jit_cases(args.ref_root)}
+              "reduction": lambda: reduction_cases(R), "batched": lambda: batched_cases(R),
+              "jit": lambda: jit_cases(args.ref_root)}
     fixtures = {}
     for name, make in groups.items():
         if args.only in (None, name):

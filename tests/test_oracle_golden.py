@@ -73,6 +73,14 @@ def test_sum_columns_golden_bit_exact(golden_dir, oracle_lib, name):
     assert np.linalg.norm(blocked - out) <= 1e-6 * np.linalg.norm(out)
 
 
+def test_bmm_golden_bit_exact(golden_dir, oracle_lib):
+    """winograd_gemm.cl:91-119 (blas.bmm): the oracle GEMM per batch entry."""
+    rec = _load(golden_dir, "bmm_42")
+    out = np.stack([O.gemm(rec["A"][i], rec["B"][i]) for i in range(rec["A"].shape[0])])
+    np.testing.assert_array_equal(out.view(np.uint32), rec["C_nofma"].view(np.uint32))
+    assert np.abs(out - rec["C_fma"]).max() < 1e-4
+
+
 def test_transpose_golden(golden_dir):
     rec = _load(golden_dir, "transpose_16x32")
     np.testing.assert_array_equal(rec["A"].T, rec["T_nofma"])
