@@ -270,6 +270,20 @@ int ojx_gemm_skinny_noalloc(const ojx_gemm_desc* d, ojx_stream s);
 int ojx_gemm_batched(const ojx_gemm_desc* d, int64_t batch, int64_t stride_a, int64_t stride_b,
                      int64_t stride_c, int64_t stride_operand, ojx_stream s);
 
+/* Scaled dot-product attention: for each of batch*heads problems,
+ *   out = softmax(scale * Q K^T) V,  Q [M, D], K and V [N, D], out [M, D], row-major,
+ * problems packed [batch][heads][rows][D].  causal: query i sees keys j <= i.  The
+ * softmax divides by (sum + 1e-6) as the reference does.  max_keys > 0 keeps only the
+ * first max_keys keys (2048 reproduces the reference kernel, whose score buffer
+ * holds 2048 entries); 0 uses all N.  dtype: F32 (GEMMs on the 3xTF32 route) or
+ * BF16/F16 (tcgen05 f16 route, P rounded to the input type).  Replaces
+ * fused_attention / run_fused_attention (torchcl/api.py:667-695,
+ * torchcl/ops/engine.py:755-773) and flash_attention.cl:8-187.  ojx_last_route
+ * reports the GEMMs' route when both took the same one. */
+int ojx_attention(void* out, const void* q, const void* k, const void* v, int32_t dtype,
+                  int64_t batch, int64_t heads, int64_t M, int64_t N, int64_t D, float scale,
+                  int32_t causal, int64_t max_keys, ojx_stream s);
+
 /* ── graph capture and replay ──────────────────────────────────────────────
  * Replaces torchcl/jit/graph_runner.py: `capture_graph` (:70-86) records the
  * launches made inside a `with` block and `CapturedGraph.replay` (:58-62)

@@ -4,6 +4,7 @@
 #include "kernels_simt.cuh"
 #include "gemm_tc.cuh"
 #include "gemm_skinny.cuh"
+#include "attention.cuh"
 #include <mutex>
 
 // ── decode GEMM for callers that cannot allocate device memory ───────────────

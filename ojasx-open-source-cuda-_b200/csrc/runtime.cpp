@@ -661,6 +661,56 @@ int ojx_cast(void* out, int32_t dtype_out, const void* in, int32_t dtype_in, int
   return launch_cast(out, dtype_out, in, dtype_in, n, static_cast<cudaStream_t>(s));
 }
 
+int ojx_attention(void* out, const void* q, const void* k, const void* v, int32_t dtype,
+                  int64_t batch, int64_t heads, int64_t M, int64_t N, int64_t D, float scale,
+                  int32_t causal, int64_t max_keys, ojx_stream stream) {
+  set_last_route(OJX_ROUTE_NONE);
+  if (batch < 0 || heads < 0 || M < 0 || N < 0 || D < 0)
+    return set_error(OJX_ERR_INVALID, "ojx_attention: negative size");
+  if (!valid_dtype(dtype)) return set_error(OJX_ERR_INVALID, "ojx_attention: unknown dtype");
+  const int64_t BH = batch * heads;
+  if (BH == 0 || M == 0 || D == 0) return OJX_OK;
+  if (!out || !q || (N > 0 && (!k || !v)))
+    return set_error(OJX_ERR_INVALID, "ojx_attention: NULL pointer");
+  if (M > INT32_MAX || N > INT32_MAX) return set_error(OJX_ERR_INVALID, "ojx_attention: too large");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t nk = max_keys > 0 && N > max_keys ? max_keys : N;
+  const int es = dtype_size(dtype);
+  if (nk == 0) {  // no keys: every output is an empty sum
+    return cuda_status(cudaMemsetAsync(out, 0, static_cast<size_t>(BH * M * D) * es, s),
+                       "attention memset");
+  }
+  const int64_t ld = (nk + 7) / 8 * 8;  // 16-byte rows for fp32 and 16-bit elements
+  const int dtype_p = dtype;            // P in the input's precision (fp32 stays fp32)
+  float* S = static_cast<float*>(
+      stream_workspace(s, static_cast<size_t>(BH * M * ld) * sizeof(float), 4, false));
+  if (!S) return workspace_error();
+  void* P = stream_workspace(s, static_cast<size_t>(BH * M * ld) * es, 5, false);
+  if (!P) return workspace_error();
+  // S = Q K^T (keys beyond nk are not read)
+  ojx_gemm_desc g{};
+  g.M = M, g.N = nk, g.K = D;
+  g.dtype_a = g.dtype_b = dtype, g.dtype_c = OJX_F32;
+  g.trans_b = 1;
+  g.lda = D, g.ldb = D, g.ldc = ld;
+  g.a = q, g.b = k, g.c = S;
+  int st = ojx_gemm_batched(&g, BH, M * D, N * D, M * ld, 0, stream);
+  if (st) return st;
+  const int route1 = t_last_route;
+  if ((st = launch_attn_softmax(S, ld, BH * M, static_cast<int>(M), static_cast<int>(nk), scale,
+                                causal ? 1 : 0, P, dtype_p, s)))
+    return st;
+  // O = P V
+  ojx_gemm_desc h{};
+  h.M = M, h.N = D, h.K = nk;
+  h.dtype_a = dtype_p, h.dtype_b = dtype, h.dtype_c = dtype;
+  h.lda = ld, h.ldb = D, h.ldc = D;
+  h.a = P, h.b = v, h.c = out;
+  st = ojx_gemm_batched(&h, BH, M * ld, N * D, M * D, 0, stream);
+  if (st == OJX_OK && route1 != t_last_route) set_last_route(OJX_ROUTE_NONE);
+  return st;
+}
+
 int ojx_sum_columns(void* out, int32_t dtype_out, const void* in, int32_t dtype_in, int64_t rows,
                     int64_t cols, int64_t ld, ojx_stream s) {
   if (rows < 0 || cols < 0) return set_error(OJX_ERR_INVALID, "ojx_sum_columns: negative size");

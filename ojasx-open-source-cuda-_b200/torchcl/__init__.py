@@ -21,7 +21,7 @@ from torchcl.api import (
     zeros, zeros_like, ones, ones_like, full, randn,
     add, sub, mul, div, neg, abs_, exp, log, sqrt, square,
     relu, sigmoid, tanh_, gelu, silu,
-    matmul, transpose, linear,
+    matmul, transpose, linear, fused_attention,
 )
 from torchcl import blas  # noqa: E402
 
@@ -31,6 +31,6 @@ __all__ = [
     "zeros", "zeros_like", "ones", "ones_like", "full", "randn",
     "add", "sub", "mul", "div", "neg", "abs_", "exp", "log", "sqrt", "square",
     "relu", "sigmoid", "tanh_", "gelu", "silu",
-    "matmul", "transpose", "linear", "blas",
+    "matmul", "transpose", "linear", "fused_attention", "blas",
     "Stream", "Event", "stream", "current_stream", "default_stream",
 ]

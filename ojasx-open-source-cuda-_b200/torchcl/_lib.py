@@ -122,6 +122,9 @@ _SIGS = {
     "ojx_cast": ([_P, ctypes.c_int32, _P, ctypes.c_int32, ctypes.c_int64, _P], ctypes.c_int),
     "ojx_gemm_batched": ([ctypes.POINTER(GemmDesc), ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                           ctypes.c_int64, ctypes.c_int64, _P], ctypes.c_int),
+    "ojx_attention": ([_P, _P, _P, _P, ctypes.c_int32, ctypes.c_int64, ctypes.c_int64,
+                       ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_float, ctypes.c_int32,
+                       ctypes.c_int64, _P], ctypes.c_int),
     "ojx_sum_columns": ([_P, ctypes.c_int32, _P, ctypes.c_int32, ctypes.c_int64, ctypes.c_int64,
                          ctypes.c_int64, _P], ctypes.c_int),
     "ojx_ipc_get_handle": ([_P, _P], ctypes.c_int),

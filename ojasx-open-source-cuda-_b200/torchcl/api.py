@@ -468,6 +468,32 @@ def transpose(a):
     return _new_lazy((shape[1], shape[0]), _get_dtype(ae), "transpose", [ae])
 
 
+def fused_attention(q, k, v, scale: float | None = None, is_causal: bool = False,
+                    max_keys: int | None = None):
+    """Scaled dot-product attention (api.py:667-695): Q [B, H, M, D], K and V
+    [B, H, N, D] -> [B, H, M, D] in Q's dtype.  `max_keys=2048` reproduces the
+    reference kernel, which only sees the first 2048 keys (flash_attention.cl:6);
+    the default uses every key."""
+    for t in (q, k, v):
+        if not is_opencl_tensor(t):
+            raise ValueError(_NOT_ON_DEVICE)
+    qs, ks, vs = _get_shape(q), _get_shape(k), _get_shape(v)
+    if len(qs) != 4 or len(ks) != 4 or ks != vs or qs[:2] != ks[:2] or qs[3] != ks[3]:
+        raise ValueError(f"fused_attention: shapes {qs}, {ks}, {vs} do not match [B,H,M,D] / [B,H,N,D]")
+    dt = _get_dtype(q)
+    if _get_dtype(k) != dt or _get_dtype(v) != dt:
+        raise ValueError("fused_attention: q, k and v must share a dtype")
+    B, H, M, D = qs
+    N = ks[2]
+    if scale is None:
+        scale = D ** -0.5
+    engine = get_engine()
+    out = engine.allocate_output((B, H, M, D), dt)
+    engine.run_fused_attention(_get_buf(q), _get_buf(k), _get_buf(v), out, B, H, M, N, D, scale,
+                               is_causal=is_causal, dtype=dt, max_keys=max_keys or 0)
+    return _wrap_output(out, (B, H, M, D), dt)
+
+
 def linear(x, weight, bias=None):
     """x @ weight^T (+ bias) — the reference's run_linear (engine.py:351-392) as one GEMM."""
     out = matmul(x, transpose(weight))

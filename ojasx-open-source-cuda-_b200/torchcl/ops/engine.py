@@ -162,6 +162,17 @@ class OpenCLEngine:
         L.check(L.lib().ojx_cast(_addr(out_buf), ojx_dtype(dtype_out), _addr(in_buf),
                                  ojx_dtype(dtype_in), int(n), get_queue()), "cast")
 
+    def run_fused_attention(self, Q, K, V, Out, B: int, H: int, M: int, N: int, D: int,
+                            scale: float, is_causal: bool = False, dtype=None,
+                            max_keys: int = 0) -> None:
+        """Out = softmax(scale * Q K^T) V per (batch, head) (engine.py:755-773):
+        two batched tcgen05 GEMMs around a row-softmax kernel."""
+        code = ojx_dtype(dtype if dtype is not None else getattr(Q, "dtype", None))
+        L.check(L.lib().ojx_attention(_addr(Out), _addr(Q), _addr(K), _addr(V), code, int(B), int(H),
+                                      int(M), int(N), int(D), float(scale), int(bool(is_causal)),
+                                      int(max_keys), get_queue()), "fused_attention")
+        self.last_route = L.ROUTES.get(L.lib().ojx_last_route(), "?")
+
     def run_sum_columns(self, input_buf, out_buf, rows: int, cols: int, dtype_in=None,
                         dtype_out=None) -> None:
         """out[cols] = input[rows, cols].sum(0) in fp32 (engine.py:807-822)."""

@@ -61,7 +61,7 @@ def build_ref(ref_root: str | os.PathLike = DEFAULT_REF_ROOT, force: bool = Fals
     """Compile the reference kernels; returns {} when the reference tree is absent."""
     kdir = ref_kernel_dir(ref_root)
     cls = {n: kdir / f"{n}.cl" for n in ("matmul", "activation", "elementwise", "precision",
-                                          "reduction", "winograd_gemm")}
+                                          "reduction", "winograd_gemm", "flash_attention")}
     if not all(p.exists() for p in cls.values()):
         return {}
     REF_OUT.mkdir(exist_ok=True)

@@ -15,6 +15,8 @@
 //    (matmul.cl:218-219).
 //  * torchcl/jit/compiler.py:33-52 (op strings) and :137-196 (kernel templates):
 //    out = u_n(...u_1(a op b)) in fp32 with libm exp/tanh/log/sqrt.
+//  * reduction.cl:170-181 sum_columns_f32 (oracle_sum_columns) and
+//    flash_attention.cl:8-187 (oracle_attention), see each function.
 // OpenCL leaves FMA contraction of `sum += a*b` to the implementation, so the
 // GEMM comes in two variants: fused == 0 rounds the product and the sum
 // separately (this file is compiled with -ffp-contract=off), fused == 1 uses one
@@ -257,6 +259,51 @@ int oracle_sum_columns(float* out, const void* in, int dt_in, int64_t rows, int6
       total = total + s;
     }
     out[c] = total;
+  }
+  return 0;
+}
+
+// Attention, as torchcl/kernels/flash_attention.cl:8-97 (flash_attention_f32) and
+// :100-187 (flash_attention_causal_f32) compute it, launched by engine.py:755-773
+// with one 256-work-item group per query row.  Per row: score[j] = (sum over k
+// ascending of q[k]*k_j[k]) * scale; (causal: only j <= row index within M; other
+// scores count as masked); max over the scores; e[j] = exp(score[j] - max); the
+// group sums e in two steps (work-item t adds e[t], e[t+256], ... in order, then
+// work-item 0 adds the 256 partial sums in order); p[j] = e[j] / (sum + 1e-6);
+// out[d] = sum over j ascending of p[j] * v_j[d].  Only keys j < 2048 take part
+// (the reference's score buffer holds 2048 entries, flash_attention.cl:6).
+// Q, K, V, out: [B*H][rows][D] fp32 (or 16-bit patterns, widened first).
+// max_keys <= 0 keeps every key instead of the reference's 2048.
+int oracle_attention(float* out, const void* q, const void* k, const void* v, int dt,
+                     int64_t BH, int64_t M, int64_t N, int64_t D, float scale, int causal,
+                     int64_t max_keys) {
+  const int64_t NK = max_keys > 0 && N > max_keys ? max_keys : N;
+#pragma omp parallel for schedule(static)
+  for (int64_t row = 0; row < BH * M; ++row) {
+    const int64_t bh = row / M, qi = row % M;
+    const int64_t nk = causal ? (qi + 1 < NK ? qi + 1 : NK) : NK;
+    std::vector<float> sc(static_cast<size_t>(nk));
+    for (int64_t j = 0; j < nk; ++j) {
+      float acc = 0.0f;
+      for (int64_t d = 0; d < D; ++d)
+        acc = acc + load(q, row * D + d, dt) * load(k, (bh * N + j) * D + d, dt);
+      sc[j] = acc * scale;
+    }
+    float mx = -1e20f;
+    for (int64_t j = 0; j < nk; ++j) mx = sc[j] > mx ? sc[j] : mx;
+    float part[256] = {0.0f};
+    for (int64_t j = 0; j < nk; ++j) {
+      sc[j] = std::exp(sc[j] - mx);
+      part[j % 256] = part[j % 256] + sc[j];
+    }
+    float sum = 0.0f;
+    for (int t = 0; t < 256; ++t) sum = sum + part[t];
+    for (int64_t j = 0; j < nk; ++j) sc[j] = sc[j] / (sum + 1e-6f);
+    for (int64_t d = 0; d < D; ++d) {
+      float acc = 0.0f;
+      for (int64_t j = 0; j < nk; ++j) acc = acc + sc[j] * load(v, (bh * N + j) * D + d, dt);
+      out[row * D + d] = acc;
+    }
   }
   return 0;
 }

@@ -52,6 +52,8 @@ def lib() -> ctypes.CDLL:
         _lib.oracle_elementwise.argtypes = [_p, _i, _p, _i, _p, _i, _i, _p, _i, _i64]
         _lib.oracle_cast.argtypes = [_p, _i, _p, _i, _i64]
         _lib.oracle_sum_columns.argtypes = [_p, _p, _i, _i64, _i64, _i64, _i64]
+        _lib.oracle_attention.argtypes = [_p, _p, _p, _p, _i, _i64, _i64, _i64, _i64,
+                                          ctypes.c_float, _i, _i64]
     return _lib
 
 
@@ -147,6 +149,22 @@ def sum_columns(x: np.ndarray, dtype_in: int = F32, block: int = 0) -> np.ndarra
     return out
 
 
+def attention(q, k, v, scale=None, causal=False, dtype: int = F32, max_keys: int = 2048):
+    """[..., M, D] x [..., N, D] attention in the reference kernel's order
+    (fp32 values or 16-bit patterns); max_keys=2048 keeps the reference's key cap,
+    0 keeps every key."""
+    q, k, v = (np.ascontiguousarray(x) for x in (q, k, v))
+    *lead, M, D = q.shape
+    N = k.shape[-2]
+    BH = int(np.prod(lead)) if lead else 1
+    if scale is None:
+        scale = D ** -0.5
+    out = np.zeros((BH, M, D), dtype=np.float32)
+    lib().oracle_attention(_ptr(out), _ptr(q), _ptr(k), _ptr(v), dtype, BH, M, N, D,
+                           float(scale), int(bool(causal)), int(max_keys))
+    return out.reshape(*lead, M, D)
+
+
 def bf16_bits(x: np.ndarray) -> np.ndarray:
     """fp32 -> bf16 bit patterns (round to nearest even)."""
     return cast(np.asarray(x, dtype=np.float32), F32, BF16)
@@ -178,6 +196,7 @@ class RefKernels:
         L.ref_unpack_fp16_to_fp32.argtypes = [_p, _p, _i]
         L.ref_sum_columns_f32.argtypes = [_p, _p, _i, _i]
         L.ref_matmul_batched_strided_f32.argtypes = [_p, _p, _p, _i, _i, _i, _i]
+        L.ref_flash_attention_f32.argtypes = [_p, _p, _p, _p, _i, _i, _i, _i, _i, ctypes.c_float, _i]
         del f32p
         self.L = L
 
@@ -208,6 +227,17 @@ class RefKernels:
         C = np.zeros((batch, M, N), dtype=np.float32)
         self.L.ref_matmul_batched_strided_f32(_ptr(A), _ptr(B), _ptr(C), batch, M, N, K)
         return C
+
+    def attention(self, q, k, v, scale=None, causal=False):
+        q, k, v = (np.ascontiguousarray(x, dtype=np.float32) for x in (q, k, v))
+        B, H, M, D = q.shape
+        N = k.shape[2]
+        if scale is None:
+            scale = D ** -0.5
+        out = np.zeros_like(q)
+        self.L.ref_flash_attention_f32(_ptr(q), _ptr(k), _ptr(v), _ptr(out), B, H, M, N, D,
+                                       float(scale), int(bool(causal)))
+        return out
 
     def sum_columns(self, X):
         X = np.ascontiguousarray(X, dtype=np.float32)

@@ -1,6 +1,6 @@
 // ref_kernels.cpp — builds the OjasX reference's own OpenCL C kernels
 // (torchcl/kernels/matmul.cl, activation.cl, elementwise.cl, precision.cl,
-// reduction.cl and winograd_gemm.cl, read from the reference tree at build time; the paths are passed
+// reduction.cl, winograd_gemm.cl and flash_attention.cl, read from the reference tree at build time; the paths are passed
 // as -D macros by oracle/build_oracle.py) for the host through clshim.h, and launches each with the
 // NDRange geometry torchcl/ops/engine.py gives it.
 // TEST INFRASTRUCTURE ONLY: output goes to oracle/_ref/ and is used to pin the
@@ -32,6 +32,9 @@ namespace cl_reduction {
 #define __local static thread_local
 namespace cl_winograd {
 #include REF_WINOGRAD_GEMM_CL
+}
+namespace cl_attention {
+#include REF_FLASH_ATTENTION_CL
 }
 
 namespace {
@@ -139,6 +142,18 @@ int ref_matmul_batched_strided_f32(const float* A, const float* B, float* C, int
   const size_t g[3] = {size_t(N), size_t(M), size_t(batch)}, l[3] = {1, 1, 1};
   clshim::run_ndrange3(g, l, [&] {
     cl_winograd::matmul_batched_strided_f32(A, B, C, batch, M, N, K, M * K, K * N, M * N);
+  });
+  return 0;
+}
+// flash_attention.cl:8-187 with engine.py:755-773's geometry: one group of 256
+// work-items per query row.
+int ref_flash_attention_f32(const float* Q, const float* K, const float* V, float* O, int B, int H,
+                            int M, int N, int D, float scale, int causal) {
+  run2(size_t(B) * H * M * 256, 1, 256, 1, [&] {
+    if (causal)
+      cl_attention::flash_attention_causal_f32(Q, K, V, O, B, H, M, N, D, scale);
+    else
+      cl_attention::flash_attention_f32(Q, K, V, O, B, H, M, N, D, scale);
   });
   return 0;
 }

@@ -6,7 +6,7 @@ Run in the development container (the reference tree is not present on GPU boxes
 the fixtures it writes are committed).  Two sources of truth are used:
 
 1. The reference's OpenCL C kernels (torchcl/kernels/matmul.cl, activation.cl,
-   precision.cl, reduction.cl, winograd_gemm.cl), compiled for the host by oracle/build_oracle.py through
+   precision.cl, reduction.cl, winograd_gemm.cl, flash_attention.cl), compiled for the host by oracle/build_oracle.py through
    oracle/ref_harness/clshim.h and launched with torchcl/ops/engine.py's geometry.
 2. The reference's JIT code generator: torchcl.jit.compiler.JITCompiler is imported
    from the reference tree (with a stand-in `pyopencl` module, since pyopencl is not
@@ -99,6 +99,22 @@ def batched_cases(R: dict) -> dict:
     B = torch.randn(4, 64, 32).numpy()
     return {"bmm_42": dict(A=A, B=B, **{f"C_{v}": r.bmm(A, B) for v, r in R.items()},
                            meta=np.array(["bmm", ""]))}
+
+
+def attention_cases(R: dict) -> dict:
+    # flash_attention.cl:8-187 through engine.py:755-773: the shapes of
+    # tests/test_fused_attention.py:9 and tests/test_cuda_correctness_baseline.py:108-111,
+    # a causal ragged case, and N > 2048 (the kernel's score buffer keeps 2048 keys).
+    out = {}
+    for seed, (B, H, M, N, D), causal in ((80, (2, 4, 32, 32, 64), False), (81, (2, 4, 16, 16, 32), False),
+                                          (82, (1, 2, 40, 40, 48), True), (83, (1, 1, 5, 2100, 32), False)):
+        q, k, v = _torch_randn(seed, B, H, M, D), _torch_randn(seed + 100, B, H, N, D), \
+            _torch_randn(seed + 200, B, H, N, D)
+        name = f"attention{'_causal' if causal else ''}_{B}x{H}x{M}x{N}x{D}"
+        out[name] = dict(q=q, k=k, v=v, causal=np.array(causal),
+                         **{f"out_{v_}": r.attention(q, k, v, causal=causal) for v_, r in R.items()},
+                         meta=np.array(["attention", ""]))
+    return out
 
 
 def reduction_cases(R: dict) -> dict:
@@ -194,7 +210,7 @@ def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref-root", default=build_oracle.DEFAULT_REF_ROOT)
     ap.add_argument("--only", default=None, help="write only the fixtures of one group "
-                    "(gemm, activation, reduction, batched, jit)")
+                    "(gemm, activation, reduction, batched, attention, jit)")
     args = ap.parse_args()
     build_oracle.build_oracle()
     if not build_oracle.build_ref(args.ref_root):
@@ -202,6 +218,7 @@ def main() -> None:
     R = {"nofma": RefKernels("nofma"), "fma": RefKernels("fma")}
     groups = {"gemm": lambda: gemm_cases(R), "activation": lambda: activation_cases(R),
               "reduction": lambda: reduction_cases(R), "batched": lambda: batched_cases(R),
+              "attention": lambda: attention_cases(R),
               "jit": lambda: jit_cases(args.ref_root)}
     fixtures = {}
     for name, make in groups.items():

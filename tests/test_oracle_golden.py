@@ -81,6 +81,16 @@ def test_bmm_golden_bit_exact(golden_dir, oracle_lib):
     assert np.abs(out - rec["C_fma"]).max() < 1e-4
 
 
+@pytest.mark.parametrize("name", ["attention_2x4x32x32x64", "attention_2x4x16x16x32",
+                                  "attention_causal_1x2x40x40x48", "attention_1x1x5x2100x32"])
+def test_attention_golden_bit_exact(golden_dir, oracle_lib, name):
+    """flash_attention.cl:8-187: the oracle's attention in the reference's order."""
+    rec = _load(golden_dir, name)
+    out = O.attention(rec["q"], rec["k"], rec["v"], causal=bool(rec["causal"]))
+    np.testing.assert_array_equal(out.view(np.uint32), rec["out_nofma"].view(np.uint32))
+    assert np.abs(out - rec["out_fma"]).max() < 1e-5
+
+
 def test_transpose_golden(golden_dir):
     rec = _load(golden_dir, "transpose_16x32")
     np.testing.assert_array_equal(rec["A"].T, rec["T_nofma"])
