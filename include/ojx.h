@@ -119,7 +119,8 @@ enum {
   OJX_ROUTE_TC_F16 = 1,   /* tcgen05 kind::f16 tile GEMM (bf16/fp16) */
   OJX_ROUTE_TC_3XTF32 = 2,/* tcgen05 kind::tf32, three MMAs per k-step */
   OJX_ROUTE_SKINNY = 3,   /* tcgen05 swap-AB stream-K skinny GEMM */
-  OJX_ROUTE_SIMT = 4      /* SIMT FMA GEMM (any shape, any stride) */
+  OJX_ROUTE_SIMT = 4,     /* SIMT FMA GEMM (any shape, any stride) */
+  OJX_ROUTE_FLASH_ATTN = 5 /* ojx_attention: fused tcgen05 attention kernel */
 };
 
 typedef struct ojx_device_info {
@@ -275,14 +276,17 @@ int ojx_gemm_batched(const ojx_gemm_desc* d, int64_t batch, int64_t stride_a, in
  * problems packed [batch][heads][rows][D].  causal: query i sees keys j <= i.  The
  * softmax divides by (sum + 1e-6) as the reference does.  max_keys > 0 keeps only the
  * first max_keys keys (2048 reproduces the reference kernel, whose score buffer
- * holds 2048 entries); 0 uses all N.  dtype: F32 (GEMMs on the 3xTF32 route) or
- * BF16/F16 (tcgen05 f16 route, P rounded to the input type).  Replaces
+ * holds 2048 entries); 0 uses all N.  bf16/fp16 with D = 64 or 128 run ONE fused
+ * kernel (tcgen05 S = QK^T and O += PV with TMEM accumulators, online softmax between
+ * them; route OJX_ROUTE_FLASH_ATTN).  Otherwise, and for fp32 (3xTF32 GEMMs), two
+ * batched GEMMs around a row-softmax kernel, P rounded to the input type.  Replaces
  * fused_attention / run_fused_attention (torchcl/api.py:667-695,
  * torchcl/ops/engine.py:755-773) and flash_attention.cl:8-187.  ojx_last_route
  * reports the GEMMs' route when both took the same one. */
 int ojx_attention(void* out, const void* q, const void* k, const void* v, int32_t dtype,
                   int64_t batch, int64_t heads, int64_t M, int64_t N, int64_t D, float scale,
-                  int32_t causal, int64_t max_keys, ojx_stream s);
+                  int32_t causal, int64_t max_keys, int32_t flags, ojx_stream s);
+#define OJX_ATTN_FLAG_COMPOSED 0x1 /* GEMM + softmax + GEMM even where the fused kernel applies */
 
 /* ── graph capture and replay ──────────────────────────────────────────────
  * Replaces torchcl/jit/graph_runner.py: `capture_graph` (:70-86) records the

@@ -5,6 +5,7 @@
 #include "gemm_tc.cuh"
 #include "gemm_skinny.cuh"
 #include "attention.cuh"
+#include "flash_attn.cuh"
 #include <mutex>
 
 // ── decode GEMM for callers that cannot allocate device memory ───────────────

@@ -663,7 +663,7 @@ int ojx_cast(void* out, int32_t dtype_out, const void* in, int32_t dtype_in, int
 
 int ojx_attention(void* out, const void* q, const void* k, const void* v, int32_t dtype,
                   int64_t batch, int64_t heads, int64_t M, int64_t N, int64_t D, float scale,
-                  int32_t causal, int64_t max_keys, ojx_stream stream) {
+                  int32_t causal, int64_t max_keys, int32_t flags, ojx_stream stream) {
   set_last_route(OJX_ROUTE_NONE);
   if (batch < 0 || heads < 0 || M < 0 || N < 0 || D < 0)
     return set_error(OJX_ERR_INVALID, "ojx_attention: negative size");
@@ -679,6 +679,13 @@ int ojx_attention(void* out, const void* q, const void* k, const void* v, int32_
   if (nk == 0) {  // no keys: every output is an empty sum
     return cuda_status(cudaMemsetAsync(out, 0, static_cast<size_t>(BH * M * D) * es, s),
                        "attention memset");
+  }
+  auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if (!(flags & OJX_ATTN_FLAG_COMPOSED) && flash_attn_supported(dtype, D) && al16(q) && al16(k) &&
+      al16(v) && al16(out)) {
+    const int st = launch_flash_attn(q, k, v, out, dtype, BH, M, N, nk, D, scale, causal ? 1 : 0, s);
+    if (st == OJX_OK) set_last_route(OJX_ROUTE_FLASH_ATTN);
+    return st;
   }
   const int64_t ld = (nk + 7) / 8 * 8;  // 16-byte rows for fp32 and 16-bit elements
   const int dtype_p = dtype;            // P in the input's precision (fp32 stays fp32)

@@ -28,7 +28,8 @@ BINARY = {"add": 1, "sub": 2, "mul": 3, "div": 4}
 OPERAND_NONE, OPERAND_ROW, OPERAND_FULL = 0, 1, 2
 FP32_AUTO, FP32_3XTF32, FP32_FFMA = 0, 1, 2
 FLAG_FORCE_SIMT, FLAG_NO_SKINNY, FLAG_FORCE_SKINNY = 0x1, 0x2, 0x4
-ROUTES = {0: "none", 1: "tc_f16", 2: "tc_3xtf32", 3: "skinny", 4: "simt"}
+ROUTES = {0: "none", 1: "tc_f16", 2: "tc_3xtf32", 3: "skinny", 4: "simt", 5: "flash_attn"}
+ATTN_FLAG_COMPOSED = 0x1
 MAX_UNARY = 8
 MAX_PEERS = 8
 IPC_HANDLE_BYTES = 64
@@ -124,7 +125,7 @@ _SIGS = {
                           ctypes.c_int64, ctypes.c_int64, _P], ctypes.c_int),
     "ojx_attention": ([_P, _P, _P, _P, ctypes.c_int32, ctypes.c_int64, ctypes.c_int64,
                        ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_float, ctypes.c_int32,
-                       ctypes.c_int64, _P], ctypes.c_int),
+                       ctypes.c_int64, ctypes.c_int32, _P], ctypes.c_int),
     "ojx_sum_columns": ([_P, ctypes.c_int32, _P, ctypes.c_int32, ctypes.c_int64, ctypes.c_int64,
                          ctypes.c_int64, _P], ctypes.c_int),
     "ojx_ipc_get_handle": ([_P, _P], ctypes.c_int),

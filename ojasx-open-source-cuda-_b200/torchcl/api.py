@@ -469,11 +469,12 @@ def transpose(a):
 
 
 def fused_attention(q, k, v, scale: float | None = None, is_causal: bool = False,
-                    max_keys: int | None = None):
+                    max_keys: int | None = None, composed: bool = False):
     """Scaled dot-product attention (api.py:667-695): Q [B, H, M, D], K and V
     [B, H, N, D] -> [B, H, M, D] in Q's dtype.  `max_keys=2048` reproduces the
     reference kernel, which only sees the first 2048 keys (flash_attention.cl:6);
-    the default uses every key."""
+    the default uses every key.  `composed=True` forces the GEMM + softmax + GEMM
+    path where the fused kernel would run (tests compare the two)."""
     for t in (q, k, v):
         if not is_opencl_tensor(t):
             raise ValueError(_NOT_ON_DEVICE)
@@ -490,7 +491,8 @@ def fused_attention(q, k, v, scale: float | None = None, is_causal: bool = False
     engine = get_engine()
     out = engine.allocate_output((B, H, M, D), dt)
     engine.run_fused_attention(_get_buf(q), _get_buf(k), _get_buf(v), out, B, H, M, N, D, scale,
-                               is_causal=is_causal, dtype=dt, max_keys=max_keys or 0)
+                               is_causal=is_causal, dtype=dt, max_keys=max_keys or 0,
+                               composed=composed)
     return _wrap_output(out, (B, H, M, D), dt)
 
 

@@ -164,14 +164,17 @@ class OpenCLEngine:
 
     def run_fused_attention(self, Q, K, V, Out, B: int, H: int, M: int, N: int, D: int,
                             scale: float, is_causal: bool = False, dtype=None,
-                            max_keys: int = 0) -> None:
-        """Out = softmax(scale * Q K^T) V per (batch, head) (engine.py:755-773):
-        two batched tcgen05 GEMMs around a row-softmax kernel."""
+                            max_keys: int = 0, composed: bool = False) -> str:
+        """Out = softmax(scale * Q K^T) V per (batch, head) (engine.py:755-773): one
+        fused tcgen05 kernel for bf16/fp16 with head dim 64/128, else two batched
+        GEMMs around a row-softmax kernel.  Returns the route."""
         code = ojx_dtype(dtype if dtype is not None else getattr(Q, "dtype", None))
         L.check(L.lib().ojx_attention(_addr(Out), _addr(Q), _addr(K), _addr(V), code, int(B), int(H),
                                       int(M), int(N), int(D), float(scale), int(bool(is_causal)),
-                                      int(max_keys), get_queue()), "fused_attention")
+                                      int(max_keys), L.ATTN_FLAG_COMPOSED if composed else 0,
+                                      get_queue()), "fused_attention")
         self.last_route = L.ROUTES.get(L.lib().ojx_last_route(), "?")
+        return self.last_route
 
     def run_sum_columns(self, input_buf, out_buf, rows: int, cols: int, dtype_in=None,
                         dtype_out=None) -> None:

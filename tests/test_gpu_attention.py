@@ -93,3 +93,32 @@ def test_attention_shape_errors():
     b = torchcl.to_opencl(torch.randn(1, 2, 4, 16))
     with pytest.raises(ValueError):
         torchcl.fused_attention(a, b, b)
+
+
+@pytest.mark.parametrize("B,H,M,N,D,causal", [(1, 2, 128, 128, 64, False), (2, 3, 200, 333, 128, False),
+                                              (1, 4, 256, 256, 128, True), (1, 2, 77, 300, 64, True),
+                                              (2, 2, 1, 1000, 128, False), (1, 1, 640, 1100, 64, True)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_fused_kernel_matches_oracle(B, H, M, N, D, causal, dtype):
+    g = torch.Generator().manual_seed(7 * M + N + D)
+    q, k, v = (torch.randn(B, H, x, D, generator=g).to(dtype) for x in (M, N, N))
+    qd, kd, vd = (torchcl.to_opencl(t) for t in (q, k, v))
+    out = torchcl.fused_attention(qd, kd, vd, is_causal=causal)
+    assert torchcl.ops.engine.get_engine().last_route == "flash_attn"
+    got = torchcl.to_cpu(out).float().numpy()
+    code = O.BF16 if dtype == torch.bfloat16 else O.F16
+    ref = O.attention(host_bits(q), host_bits(k), host_bits(v), causal=causal, dtype=code, max_keys=0)
+    assert rel_l2(got, ref) <= 1e-2, rel_l2(got, ref)
+    composed = torchcl.to_cpu(torchcl.fused_attention(qd, kd, vd, is_causal=causal, composed=True))
+    assert rel_l2(got, composed.float().numpy()) <= 1e-2
+
+
+def test_fused_kernel_one_launch_and_key_limit():
+    g = torch.Generator().manual_seed(11)
+    q, k, v = (torch.randn(1, 2, x, 64, generator=g).bfloat16() for x in (64, 2300, 2300))
+    qd, kd, vd = (torchcl.to_opencl(t) for t in (q, k, v))
+    n0 = L.lib().ojx_kernel_launch_count()
+    capped = torchcl.to_cpu(torchcl.fused_attention(qd, kd, vd, max_keys=2048)).float().numpy()
+    assert L.lib().ojx_kernel_launch_count() - n0 == 1
+    ref = O.attention(host_bits(q), host_bits(k), host_bits(v), dtype=O.BF16, max_keys=2048)
+    assert rel_l2(capped, ref) <= 1e-2
