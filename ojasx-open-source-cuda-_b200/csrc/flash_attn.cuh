@@ -7,16 +7,18 @@
 //                computed, V_j's after PV_j, so K_{j+2} loads while PV_j runs.
 //   warp 1       MMA issuer: S_j = Q K_j^T into one of two TMEM score buffers
 //                (S_{j+1} is issued before PV_j so it overlaps the softmax of S_j),
-//                then O += P_j V_j into the TMEM output accumulator
+//                then O += P_j V_j into the TMEM output accumulator, with P_j read
+//                from TMEM (it overwrites the first half of S_j's buffer).  One
+//                thread issues every MMA, in order, so S_{j+2} cannot overwrite
+//                P_j before PV_j has read it.
 //   warps 2-9    softmax: warp w owns TMEM lane quarter w%4 (one query row per
 //                thread) and key half (w-2)/4 of each tile (two warps per scheduler
 //                hide each other's latency).  The two threads of a row exchange
 //                their tile maxima through shared memory; each keeps its half of
-//                the scores in registers, writes its half of P_j (16-bit, the
-//                128-byte-swizzled K-major layout the MMA reads), rescales its half
-//                of the row's O in TMEM when the max grows by more than 2^8, and
-//                stores its half of the final O / (sum + 1e-6) (the reference's
-//                denominator) to HBM
+//                the scores in registers, stores its half of P_j as packed 16-bit
+//                pairs into TMEM, rescales its half of the row's O in TMEM when the
+//                max grows by more than 2^8, and stores its half of the final
+//                O / (sum + 1e-6) (the reference's denominator) to HBM
 //
 // Semantics are flash_attention.cl:8-187's: scores = scale * q.k, causal keeps
 // key j <= query i (top-left aligned), keys >= nk are ignored.
@@ -39,12 +41,12 @@ struct FaLayout {
   static constexpr int Q_BYTES = FA_BM * D * 2;        // DB sub-tiles of 128 rows x 128 B
   static constexpr int K_BYTES = FA_BN * D * 2;
   static constexpr int V_BYTES = FA_BN * D * 2;        // 2 key blocks x DB d blocks of 64 x 64
-  static constexpr int P_BYTES = FA_BM * FA_BN * 2;    // 2 key blocks of 128 rows x 128 B
   static constexpr int STAGE_BYTES = K_BYTES + V_BYTES;
   static constexpr int XCH_BYTES = 6 * FA_BM * 4;     // row maxima (2 buffers x 2 halves), row sums
   static constexpr int BAR_BYTES = 256;
-  static constexpr int SMEM = Q_BYTES + FA_ST * STAGE_BYTES + P_BYTES + XCH_BYTES + BAR_BYTES + 1024;
-  static constexpr uint32_t TMEM_COLS = 512;           // S0 [0,128), S1 [128,256), O [256,256+D)
+  static constexpr int SMEM = Q_BYTES + FA_ST * STAGE_BYTES + XCH_BYTES + BAR_BYTES + 1024;
+  // S0 [0,128), S1 [128,256) (P_j packed into the first 64 columns of S_j's), O [256,256+D)
+  static constexpr uint32_t TMEM_COLS = 512;
 };
 
 // 2^x on the special-function unit (flush-to-zero: P is rounded to 16 bits, and a
@@ -74,10 +76,8 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
   const uint32_t sbase = smem_u32(smem);
   const uint32_t sQ = sbase;
   const uint32_t sKV = sQ + L::Q_BYTES;
-  const uint32_t sP = sKV + FA_ST * L::STAGE_BYTES;
-  float* xch = reinterpret_cast<float*>(smem + L::Q_BYTES + FA_ST * L::STAGE_BYTES + L::P_BYTES);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::Q_BYTES + FA_ST * L::STAGE_BYTES + L::P_BYTES +
-                                               L::XCH_BYTES);
+  float* xch = reinterpret_cast<float*>(smem + L::Q_BYTES + FA_ST * L::STAGE_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::Q_BYTES + FA_ST * L::STAGE_BYTES + L::XCH_BYTES);
   const uint32_t bar0 = smem_u32(bars);
   // barrier slots
   const uint32_t q_full = bar0;
@@ -86,7 +86,6 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
   auto v_full = [&](int s) { return bar0 + 8u * (1 + 2 * FA_ST + s); };
   auto v_empty = [&](int s) { return bar0 + 8u * (1 + 3 * FA_ST + s); };
   auto s_full = [&](int b) { return bar0 + 8u * (1 + 4 * FA_ST + b); };
-  auto s_empty = [&](int b) { return bar0 + 8u * (3 + 4 * FA_ST + b); };
   const uint32_t p_full = bar0 + 8u * (5 + 4 * FA_ST);
   const uint32_t pv_done = bar0 + 8u * (6 + 4 * FA_ST);
   const uint32_t done_bar = bar0 + 8u * (7 + 4 * FA_ST);
@@ -110,10 +109,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       mbar_init(v_full(s), 1);
       mbar_init(v_empty(s), 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(s_full(b), 1);
-      mbar_init(s_empty(b), 8);
-    }
+    for (int b = 0; b < 2; ++b) mbar_init(s_full(b), 1);
     mbar_init(p_full, 8);
     mbar_init(pv_done, 1);
     mbar_init(done_bar, 1);
@@ -182,9 +178,8 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       bool ok = mbar_wait(q_full, 0, p.budget, s_abort);
       auto issue_s = [&](int j) {
         const int st = j % FA_ST, buf = j & 1;
+        // S_j reuses the buffer of P_{j-2}: PV_{j-2} was issued before, by this thread
         if (!mbar_wait(k_full(st), static_cast<uint32_t>(j / FA_ST) & 1u, p.budget, s_abort)) return false;
-        if (!mbar_wait(s_empty(buf), (static_cast<uint32_t>(j >> 1) & 1u) ^ 1u, p.budget, s_abort))
-          return false;
         tc_fence_after();
         const uint32_t sK = sKV + st * L::STAGE_BYTES;
 #pragma unroll
@@ -205,12 +200,12 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
         if (!mbar_wait(p_full, static_cast<uint32_t>(j) & 1u, p.budget, s_abort)) break;
         tc_fence_after();
         const uint32_t sV = sKV + st * L::STAGE_BYTES + L::K_BYTES;
+        const uint32_t p_tmem = tmem + (j & 1) * FA_BN;  // P_j: 16 keys per 8 columns
 #pragma unroll
         for (int ks = 0; ks < FA_BN / 16; ++ks) {
-          const uint64_t a = make_sw128_desc(sP + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024);
           const uint64_t b =
               make_sw128_desc(sV + (ks >> 2) * (L::DB * 8192) + (ks & 3) * 2048, 8192, 1024);
-          mma_f16(tmem + 2 * FA_BN, a, b, IDESC_PV, (j > 0 || ks > 0) ? 1u : 0u);
+          mma_f16_ts(tmem + 2 * FA_BN, p_tmem + ks * 8, b, IDESC_PV, (j > 0 || ks > 0) ? 1u : 0u);
         }
         mma_commit(pv_done);
         mma_commit(v_empty(st));
@@ -244,16 +239,12 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       int n_vis = min(FA_BN, p.nk - key0);
       if (p.causal) n_vis = min(n_vis, qi - key0 + 1);
       n_vis -= 64 * half;
-      // this thread's half of the score row: 4 loads, one wait; then the S buffer is
-      // free for S_{j+2}
+      // this thread's half of the score row: 4 loads, one wait
       uint32_t r[HK];
 #pragma unroll
       for (int c = 0; c < HK; c += 16)
         tmem_ld16(trow + buf * FA_BN + 64 * half + c, *reinterpret_cast<uint32_t(*)[16]>(&r[c]));
       tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(s_empty(buf));
       // Row maximum (log2 domain).  The running maximum is only raised when the
       // tile's exceeds it by more than 8 (a factor 256): terms stay below 2^8, and
       // the output accumulator is rescaled only on those rare steps.  Maxima and
@@ -271,7 +262,8 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       }
       float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                        fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
-      // the row's maximum over both halves (double-buffered exchange slot)
+      // the row's maximum over both halves (double-buffered exchange slot); after
+      // this barrier both halves have read their scores, so P may overwrite them
       {
         float* slot = xch + ((j & 1) * 2) * FA_BM;
         slot[half * FA_BM + row] = mx;
@@ -310,7 +302,13 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
                         ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
       l_run = l_run * alpha + sum;
       m_run = m_new;
-      // PV_{j-1} must be done: it read the P buffer and wrote O
+      // P_j into the first 64 columns of S_j's buffer: this half's 64 keys are
+      // 32 packed columns at 32 * half
+#pragma unroll
+      for (int c = 0; c < HK / 2; c += 16)
+        tmem_st16(trow + buf * FA_BN + 32 * half + c, *reinterpret_cast<const uint32_t(*)[16]>(&pk[c]));
+      // PV_{j-1} must be done before O is rescaled (and PV_j waits for this tile's
+      // arrival below); usually it finished while the exponentials were computed
       if (j > 0) {
         const bool w2 = mbar_wait(pv_done, static_cast<uint32_t>(j - 1) & 1u, p.budget, s_abort);
         if (named_bar_red_or(1, FA_SMX, !w2)) {
@@ -318,14 +316,6 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
           break;
         }
         tc_fence_after();
-      }
-      // keys 64 half + 8c .. +7 = 16-byte chunk c of key block `half` (128-byte swizzle)
-#pragma unroll
-      for (int c = 0; c < HK / 8; ++c) {
-        const uint32_t a = sP + half * 16384 + row * 128 + ((c ^ (row & 7)) << 4);
-        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(pk[4 * c]),
-                     "r"(pk[4 * c + 1]), "r"(pk[4 * c + 2]), "r"(pk[4 * c + 3])
-                     : "memory");
       }
       // rescale this half of the rows whose maximum was raised (warp-wide collective access)
       if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
@@ -338,9 +328,8 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
           for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
           tmem_st16(trow + o_col + c, o);
         }
-        tmem_wait_st();
       }
-      fence_proxy_async_smem();  // P (generic-proxy stores) -> visible to the MMA
+      tmem_wait_st();  // P_j (and a rescaled O) written before PV_j may read them
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);

@@ -168,6 +168,17 @@ __device__ __forceinline__ void tc_fence_after() {
 }
 
 // D(tmem) (+)= A(smem desc) * B(smem desc), kind::f16 (bf16 or fp16 inputs, fp32 accumulate).
+// The same MMA with its A operand (M rows = TMEM lanes, K packed two 16-bit
+// elements per 32-bit column) read from tensor memory at column address a_tmem.
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                           uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
                                         uint32_t idesc, uint32_t accumulate) {
   asm volatile(
