@@ -226,13 +226,10 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
     constexpr int HK = FA_BN / 2;  // keys per thread
     float m_run = -INFINITY, l_run = 0.0f;
     bool ok = true;
+    bool failed = false;  // a bounded wait of this thread gave up; agreed at the next barrier
     for (int j = 0; j < kv_tiles; ++j) {
       const int buf = j & 1;
-      const bool waited = mbar_wait(s_full(buf), static_cast<uint32_t>(j >> 1) & 1u, p.budget, s_abort);
-      if (named_bar_red_or(1, FA_SMX, !waited)) {
-        ok = false;
-        break;
-      }
+      failed |= !mbar_wait(s_full(buf), static_cast<uint32_t>(j >> 1) & 1u, p.budget, s_abort);
       tc_fence_after();
       const int key0 = j * FA_BN;
       // keys of this row in this thread's half: [key0 + 64 half, key0 + 64 half + n_vis)
@@ -263,11 +260,16 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                        fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       // the row's maximum over both halves (double-buffered exchange slot); after
-      // this barrier both halves have read their scores, so P may overwrite them
+      // this barrier both halves have read their scores, so P may overwrite them.
+      // The same barrier makes every softmax warp agree on stopping when any wait
+      // gave up (the loop's only other barrier use is the next tile's).
       {
         float* slot = xch + ((j & 1) * 2) * FA_BM;
         slot[half * FA_BM + row] = mx;
-        named_bar_sync(1, FA_SMX);
+        if (named_bar_red_or(1, FA_SMX, failed)) {
+          ok = false;
+          break;
+        }
         mx = fmaxf(mx, slot[(1 - half) * FA_BM + row]);
       }
       mx *= p.scale_log2;  // scale > 0: the maximum of the scaled scores
@@ -309,16 +311,14 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
         tmem_st16(trow + buf * FA_BN + 32 * half + c, *reinterpret_cast<const uint32_t(*)[16]>(&pk[c]));
       // PV_{j-1} must be done before O is rescaled (and PV_j waits for this tile's
       // arrival below); usually it finished while the exponentials were computed
+      bool o_ready = true;
       if (j > 0) {
-        const bool w2 = mbar_wait(pv_done, static_cast<uint32_t>(j - 1) & 1u, p.budget, s_abort);
-        if (named_bar_red_or(1, FA_SMX, !w2)) {
-          ok = false;
-          break;
-        }
+        o_ready = mbar_wait(pv_done, static_cast<uint32_t>(j - 1) & 1u, p.budget, s_abort);
+        failed |= !o_ready;
         tc_fence_after();
       }
       // rescale this half of the rows whose maximum was raised (warp-wide collective access)
-      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+      if (j > 0 && __all_sync(0xffffffffu, o_ready) && __any_sync(0xffffffffu, alpha != 1.0f)) {
 #pragma unroll 1
         for (int c = half * (D / 2); c < (half + 1) * (D / 2); c += 16) {
           uint32_t o[16];
@@ -339,7 +339,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
     if (have_o) {
       const bool w3 =
           mbar_wait(pv_done, static_cast<uint32_t>(kv_tiles - 1) & 1u, p.budget, s_abort);
-      have_o = !named_bar_red_or(1, FA_SMX, !w3);
+      have_o = !named_bar_red_or(1, FA_SMX, !w3 || failed);
       if (have_o) tc_fence_after();
     }
     // the row's sum over both halves (its own slots: a partner may still read the
