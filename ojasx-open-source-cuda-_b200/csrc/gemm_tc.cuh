@@ -68,7 +68,7 @@ struct TcLayout {
 
 // Grouped raster: 8 consecutive M-blocks share each N-block sweep.
 __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int& mb, int& nb) {
-  constexpr int GROUP = 8;
+  constexpr int GROUP = 16;
   const int span = GROUP * tiles_n;
   const int g = tile / span;
   const int first_m = g * GROUP;
