@@ -329,7 +329,8 @@ def run_ours(args, cfg, world, rank, local):
     value = flops_total * args.steps / (total_ms / 1e3) / 1e12
 
     # e2e through the C-ABI with pinned host buffers
-    e2e = e2e_measure(args, lib, L, A, C, M, K, N, es, gemm, gather, world, dev, stream)
+    e2e = e2e_measure(args, lib, L, A, C, M, K, N, es, gemm, gather, world, dev, stream,
+                      desc=d if sharded is None else None)
 
     peaks, peak_kind = _peaks()
     avg_gemm_ms = statistics.mean(gemm_ms)
@@ -381,8 +382,11 @@ def run_ours(args, cfg, world, rank, local):
     return 0
 
 
-def e2e_measure(args, lib, L, A, C, M, K, N, es, gemm, gather, world, dev, stream):
-    """Same metric end to end: pinned host A -> device, GEMM (+gather), C -> pinned host."""
+def e2e_measure(args, lib, L, A, C, M, K, N, es, gemm, gather, world, dev, stream, desc=None):
+    """Same metric end to end: pinned host A -> device, GEMM (+gather), C -> pinned host.
+    On one GPU through ojx_gemm_host_io (chunks of rows: uploads, GEMMs and downloads
+    overlap on three streams); on several, upload, sharded GEMM with the gather, barrier
+    and download one after another."""
     import torch
     import torch.distributed as dist
     a_bytes = M * K * es
@@ -395,11 +399,19 @@ def e2e_measure(args, lib, L, A, C, M, K, N, es, gemm, gather, world, dev, strea
     L.check(lib.ojx_memcpy_d2h(ha.value, A.data_ptr(), a_bytes, sp))
     torch.cuda.synchronize(dev)
 
-    def step():
-        L.check(lib.ojx_memcpy_h2d(A.data_ptr(), ha.value, a_bytes, sp), "h2d")
-        gemm()
-        gather()
-        L.check(lib.ojx_memcpy_d2h(hc.value, C.data_ptr(), c_bytes, sp), "d2h")
+    if desc is not None:
+        dh = L.GemmDesc.from_buffer_copy(desc)
+        dh.a, dh.c = ha.value, hc.value
+
+        def step():
+            L.check(lib.ojx_gemm_host_io(ctypes.byref(dh), A.data_ptr(), C.data_ptr(), 0, sp),
+                    "gemm_host_io")
+    else:
+        def step():
+            L.check(lib.ojx_memcpy_h2d(A.data_ptr(), ha.value, a_bytes, sp), "h2d")
+            gemm()
+            gather()
+            L.check(lib.ojx_memcpy_d2h(hc.value, C.data_ptr(), c_bytes, sp), "d2h")
 
     steps = max(2, min(args.steps, 5))
     step()
@@ -423,7 +435,10 @@ def e2e_measure(args, lib, L, A, C, M, K, N, es, gemm, gather, world, dev, strea
     flops = 2.0 * M * N * K * steps
     return {"value": flops / dt / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": a_bytes,
             "d2h_bytes_per_step": c_bytes, "steps": steps,
-            "note": "C-ABI with pinned host buffers; CUDA events on the launching stream, max over ranks"}
+            "note": ("ojx_gemm_host_io (C-ABI, pinned host A and C, chunked: copies overlap the GEMM)"
+                     if desc is not None else
+                     "C-ABI with pinned host buffers: upload, GEMM + gather, download; max over ranks")
+            + "; CUDA events on the launching stream"}
 
 
 def run_train(args, cfg):

@@ -271,6 +271,20 @@ int ojx_gemm_skinny_noalloc(const ojx_gemm_desc* d, ojx_stream s);
 int ojx_gemm_batched(const ojx_gemm_desc* d, int64_t batch, int64_t stride_a, int64_t stride_b,
                      int64_t stride_c, int64_t stride_operand, ojx_stream s);
 
+/* The GEMM with A and C in host memory (pinned, for the overlap) and B and the epilogue
+ * operand on the device: the rows are processed in chunks (chunk_rows, or 0 for about
+ * eight chunks of whole 128-row tile blocks); chunk i+1 uploads into dev_a, chunk i
+ * computes into dev_c and chunk i-1 downloads, on three library streams, so only the
+ * first upload and the last download are not hidden behind GEMM work.  dev_a ([M,K])
+ * and dev_c ([M,N]) are caller-owned device buffers; A and C must be dense row-major.
+ * Ordered after the work already queued on `s`; `s` waits for the last download, so
+ * synchronising `s` means C is in host memory.  Replaces the upload / matmul / download
+ * sequence of to_opencl + matmul + to_cpu (torchcl/api.py:210-232, 427-469), which the
+ * reference runs one after another with a blocking copy on each side
+ * (torchcl/runtime/memory.py:145-177). */
+int ojx_gemm_host_io(const ojx_gemm_desc* d, void* dev_a, void* dev_c, int64_t chunk_rows,
+                     ojx_stream s);
+
 /* Scaled dot-product attention: for each of batch*heads problems,
  *   out = softmax(scale * Q K^T) V,  Q [M, D], K and V [N, D], out [M, D], row-major,
  * problems packed [batch][heads][rows][D].  causal: query i sees keys j <= i.  The

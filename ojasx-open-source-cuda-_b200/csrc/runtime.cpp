@@ -615,6 +615,113 @@ int ojx_gemm_batched(const ojx_gemm_desc* in, int64_t batch, int64_t stride_a, i
   return OJX_OK;
 }
 
+}  // extern "C"
+
+namespace ojx {
+namespace {
+// Streams and events of ojx_gemm_host_io, one set per device.
+struct IoStreams {
+  cudaStream_t h2d = nullptr, comp = nullptr, d2h = nullptr;
+  std::vector<cudaEvent_t> ev;
+  std::mutex mu;  // one call at a time issues on these streams
+};
+IoStreams* io_streams(int dev) {
+  static std::mutex mu;
+  static std::map<int, IoStreams*>* m = new std::map<int, IoStreams*>();
+  std::lock_guard<std::mutex> g(mu);
+  IoStreams*& io = (*m)[dev];
+  if (!io) {
+    auto* n = new IoStreams();
+    if (cudaStreamCreateWithFlags(&n->h2d, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&n->comp, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&n->d2h, cudaStreamNonBlocking) != cudaSuccess) {
+      (void)cudaGetLastError();
+      delete n;
+      return nullptr;
+    }
+    io = n;
+  }
+  return io;
+}
+int io_events(IoStreams* io, size_t n) {
+  while (io->ev.size() < n) {
+    cudaEvent_t e;
+    if (int st = cuda_status(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate"))
+      return st;
+    io->ev.push_back(e);
+  }
+  return OJX_OK;
+}
+}  // namespace
+}  // namespace ojx
+
+extern "C" {
+
+int ojx_gemm_host_io(const ojx_gemm_desc* in, void* dev_a, void* dev_c, int64_t chunk_rows,
+                     ojx_stream stream) {
+  set_last_route(OJX_ROUTE_NONE);
+  ojx_gemm_desc d;
+  int st = prepare_desc(in, &d, "ojx_gemm_host_io");
+  if (st == kEmptyProblem) return OJX_OK;
+  if (st) return st;
+  if (!dev_a || !dev_c) return set_error(OJX_ERR_INVALID, "ojx_gemm_host_io: NULL staging buffer");
+  if (d.trans_a || d.lda != d.K || d.ldc != d.N)
+    return set_error(OJX_ERR_INVALID,
+                     "ojx_gemm_host_io: A must be row-major [M,K] and C [M,N], both dense");
+  int dev = 0;
+  if ((st = cuda_status(cudaGetDevice(&dev), "cudaGetDevice"))) return st;
+  IoStreams* io = io_streams(dev);
+  if (!io) return set_error(OJX_ERR_CUDA, "ojx_gemm_host_io: cannot create its streams");
+  std::lock_guard<std::mutex> g(io->mu);
+  const int64_t M = d.M;
+  // Chunks of whole 128-row tile blocks: about 8 of them, so the first upload and
+  // the last download (the parts not hidden behind a GEMM) stay small.
+  int64_t rows = chunk_rows > 0 ? chunk_rows : ((M + 7) / 8 + 127) / 128 * 128;
+  if (rows >= M || M <= 256) rows = M;
+  const int64_t n_chunks = (M + rows - 1) / rows;
+  if ((st = io_events(io, static_cast<size_t>(2 * n_chunks + 2)))) return st;
+  cudaEvent_t* ev = io->ev.data();
+  const size_t ea = dtype_size(d.dtype_a), ec = dtype_size(d.dtype_c), eo = dtype_size(d.dtype_operand);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // everything after the work already queued on the caller's stream
+  if ((st = cuda_status(cudaEventRecord(ev[0], s), "event record"))) return st;
+  for (cudaStream_t x : {io->h2d, io->comp, io->d2h})
+    if ((st = cuda_status(cudaStreamWaitEvent(x, ev[0], 0), "stream wait"))) return st;
+  int route = OJX_ROUTE_NONE;
+  for (int64_t c = 0; c < n_chunks; ++c) {
+    const int64_t r0 = c * rows, nr = std::min(rows, M - r0);
+    char* da = static_cast<char*>(dev_a) + static_cast<size_t>(r0 * d.K) * ea;
+    char* dc = static_cast<char*>(dev_c) + static_cast<size_t>(r0 * d.N) * ec;
+    const char* ha = static_cast<const char*>(d.a) + static_cast<size_t>(r0 * d.K) * ea;
+    char* hc = static_cast<char*>(d.c) + static_cast<size_t>(r0 * d.N) * ec;
+    cudaEvent_t up = ev[2 + 2 * c], done = ev[3 + 2 * c];
+    if ((st = cuda_status(cudaMemcpyAsync(da, ha, static_cast<size_t>(nr * d.K) * ea,
+                                          cudaMemcpyHostToDevice, io->h2d), "chunk upload")) ||
+        (st = cuda_status(cudaEventRecord(up, io->h2d), "event record")) ||
+        (st = cuda_status(cudaStreamWaitEvent(io->comp, up, 0), "stream wait")))
+      return st;
+    ojx_gemm_desc dd = d;
+    dd.M = nr;
+    dd.a = da;
+    dd.c = dc;
+    if (d.operand_kind == OJX_OPERAND_FULL)
+      dd.operand = static_cast<const char*>(d.operand) + static_cast<size_t>(r0 * d.ld_operand) * eo;
+    if ((st = gemm_one(dd, io->comp))) return st;
+    route = t_last_route;
+    if ((st = cuda_status(cudaEventRecord(done, io->comp), "event record")) ||
+        (st = cuda_status(cudaStreamWaitEvent(io->d2h, done, 0), "stream wait")) ||
+        (st = cuda_status(cudaMemcpyAsync(hc, dc, static_cast<size_t>(nr * d.N) * ec,
+                                          cudaMemcpyDeviceToHost, io->d2h), "chunk download")))
+      return st;
+  }
+  // the caller's stream continues once C is in host memory
+  if ((st = cuda_status(cudaEventRecord(ev[1], io->d2h), "event record")) ||
+      (st = cuda_status(cudaStreamWaitEvent(s, ev[1], 0), "stream wait")))
+    return st;
+  set_last_route(route);
+  return OJX_OK;
+}
+
 int ojx_elementwise(void* out, int32_t dtype_out, const void* a, int32_t dtype_a, const void* b,
                     int32_t dtype_b, int32_t binary_op, const int32_t* unary, int32_t n_unary,
                     int64_t n, ojx_stream s) {

@@ -123,6 +123,7 @@ _SIGS = {
     "ojx_cast": ([_P, ctypes.c_int32, _P, ctypes.c_int32, ctypes.c_int64, _P], ctypes.c_int),
     "ojx_gemm_batched": ([ctypes.POINTER(GemmDesc), ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                           ctypes.c_int64, ctypes.c_int64, _P], ctypes.c_int),
+    "ojx_gemm_host_io": ([ctypes.POINTER(GemmDesc), _P, _P, ctypes.c_int64, _P], ctypes.c_int),
     "ojx_attention": ([_P, _P, _P, _P, ctypes.c_int32, ctypes.c_int64, ctypes.c_int64,
                        ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_float, ctypes.c_int32,
                        ctypes.c_int64, ctypes.c_int32, _P], ctypes.c_int),

@@ -101,3 +101,62 @@ def test_launch_counter_and_device_info():
     B = randn(6, (64, 128), torch.bfloat16)
     run_gemm(A, B, flags=0x2)
     assert lib.ojx_kernel_launch_count() == n0 + 1
+
+
+@pytest.mark.parametrize("M,N,K,dtype,chunk", [(1000, 512, 256, torch.bfloat16, 256),
+                                               (4096, 1024, 512, torch.bfloat16, 0),
+                                               (700, 384, 200, torch.float32, 128),
+                                               (8, 2048, 1024, torch.bfloat16, 0)])
+def test_gemm_host_io_matches_device_gemm(M, N, K, dtype, chunk):
+    """ojx_gemm_host_io (host A and C, rows in overlapped chunks) gives exactly the
+    device-resident GEMM's output: every row's accumulation is the same."""
+    torchcl.init_opencl()
+    lib = L.lib()
+    A = randn(1, (M, K), dtype)
+    W = randn(2, (K, N), dtype, scale=0.05)
+    bias = randn(3, (N,), dtype, scale=0.1)
+    es = A.element_size()
+    dev = torch.device("cuda", 0)
+    Wd, bd = W.to(dev), bias.to(dev)
+    Ad = torch.empty(M, K, dtype=dtype, device=dev)
+    Cd = torch.empty(M, N, dtype=dtype, device=dev)
+    ha, hc = ctypes.c_void_p(), ctypes.c_void_p()
+    L.check(lib.ojx_host_alloc(M * K * es, ctypes.byref(ha)))
+    L.check(lib.ojx_host_alloc(M * N * es, ctypes.byref(hc)))
+    try:
+        ctypes.memmove(ha.value, A.contiguous().data_ptr(), M * K * es)
+        code = L.BF16 if dtype == torch.bfloat16 else L.F32
+        d = L.GemmDesc()
+        d.M, d.N, d.K = M, N, K
+        d.dtype_a = d.dtype_b = d.dtype_c = d.dtype_operand = code
+        d.b, d.operand = Wd.data_ptr(), bd.data_ptr()
+        d.operand_kind, d.binary_op = L.OPERAND_ROW, L.BINARY["add"]
+        d.n_unary, d.unary[0] = 1, L.UNARY["relu"]
+        d.a, d.c = ha.value, hc.value
+        L.check(lib.ojx_gemm_host_io(ctypes.byref(d), Ad.data_ptr(), Cd.data_ptr(), chunk, None))
+        L.check(lib.ojx_synchronize())
+        got = torch.empty(M, N, dtype=dtype)
+        ctypes.memmove(got.data_ptr(), hc.value, M * N * es)
+        # the same GEMM on device-resident operands
+        Ad2 = A.to(dev)
+        Cd2 = torch.empty(M, N, dtype=dtype, device=dev)
+        d.a, d.c = Ad2.data_ptr(), Cd2.data_ptr()
+        L.check(lib.ojx_gemm(ctypes.byref(d), None))
+        L.check(lib.ojx_synchronize())
+        assert torch.equal(got, Cd2.cpu())
+        ref = oracle_gemm(A, W, operand=bias, kind="row", unary=("relu",))
+        if dtype == torch.bfloat16:
+            assert_half_parity(got.float().numpy(), ref)
+    finally:
+        lib.ojx_host_free(ha.value)
+        lib.ojx_host_free(hc.value)
+
+
+def test_gemm_host_io_rejects_strided_operands():
+    torchcl.init_opencl()
+    lib = L.lib()
+    d = L.GemmDesc()
+    d.M, d.N, d.K = 64, 64, 64
+    d.a = d.b = d.c = 16
+    d.lda = 128
+    assert lib.ojx_gemm_host_io(ctypes.byref(d), 16, 16, 0, None) == L.OJX_ERR_INVALID
