@@ -24,6 +24,14 @@
 // last arriver also stores 0 into its counter, so a completed launch leaves the
 // counters as it found them: a launch replayed from a CUDA graph (same epoch
 // every time) then starts from zero as well.
+//
+// Back-to-back decode launches (one per layer) overlap through programmatic
+// dependent launch: each grid lets the next one start as soon as it is resident,
+// and the next grid's CTAs, placed as this grid's CTAs exit, set up and prefetch
+// their first SK_PREFETCH units of W into L2 before griddepcontrol.wait.  Every
+// other global access (X, the epilogue operand, C, the scratch) comes after that
+// wait, so it sees all of the previous kernel's writes.  HBM then keeps streaming
+// across the previous launch's split-K tail instead of idling through it.
 #include <cuda_runtime.h>
 #include <algorithm>
 #include "sm100.cuh"
@@ -43,6 +51,7 @@ constexpr int SK_W_BYTES = SK_TPU * SK_BN * 128;
 constexpr int SK_X_BYTES = SK_MN * 128;
 constexpr int SK_STAGE_BYTES = SK_W_BYTES + SK_X_BYTES;
 constexpr int SK_NBUF = 4;  // TMEM accumulator buffers (segments in flight)
+constexpr int SK_PREFETCH = 8;  // units of W fetched into L2 before the dependency wait
 constexpr uint32_t SK_TMEM_COLS = SK_NBUF * SK_TPU * SK_MN;
 constexpr int SK_SLOT = SK_TPU * SK_MN * SK_BN;  // floats per partial slot
 constexpr int SK_EPI_BYTES = SK_TPU * SK_MN * SK_BN * 4;  // finished block, fp32
@@ -125,6 +134,9 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *s_tmem;
+  // Every CTA of this grid is resident: the next launch may begin.  Its CTAs only
+  // find room on an SM once this grid's CTA there has exited.
+  grid_dep_launch_dependents();
 
   const long long ub = unit_begin(blockIdx.x, p);
   const long long ue = unit_begin(blockIdx.x + 1, p);
@@ -135,6 +147,27 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
   if (warp == 0) {
     // ── TMA producer ────────────────────────────────────────────────────
     if (lane == 0 && !p.silence_producer) {
+      {  // W tiles of the first units into L2 while the previous grid finishes
+        int g = g_begin, kb = kb_begin;
+        const int npf = min(n_units, SK_PREFETCH);
+        for (int i = 0; i < npf; ++i) {
+          const int n0 = g * (SK_TPU * SK_BN), k0 = kb * SK_BK;
+#pragma unroll
+          for (int j = 0; j < SK_TPU; ++j) {
+            if (W_MN) {
+              tma_prefetch_l2_2d(&tmW, n0 + j * SK_BN, k0);
+              tma_prefetch_l2_2d(&tmW, n0 + j * SK_BN + 64, k0);
+            } else {
+              tma_prefetch_l2_2d(&tmW, k0, n0 + j * SK_BN);
+            }
+          }
+          if (++kb == p.KB) {
+            kb = 0;
+            ++g;
+          }
+        }
+      }
+      grid_dep_wait();
       int stage = 0, g = g_begin, kb = kb_begin;
       uint32_t phase = 0, issued = 0, issued_parity = 0;
       for (int i = 0; i < n_units; ++i) {
@@ -170,6 +203,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
   } else if (warp == 1) {
     // ── MMA issuer ──────────────────────────────────────────────────────
     if (lane == 0) {
+      grid_dep_wait();  // the bounded waits below start once the inputs are final
       constexpr uint32_t IDESC = make_idesc(FMT, W_MN, 0, SK_BN, SK_MN);
       int stage = 0, acc = 0, kb = kb_begin;
       uint32_t phase = 0, acc_phase = 0;
@@ -220,6 +254,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
     // ── epilogue: 128 threads, thread <-> one column of each tile of the group
     const int q = warp & 3;
     const int etid = threadIdx.x - 64;  // 0..127
+    grid_dep_wait();  // the operand, C and the scratch may belong to the previous kernel
     int acc = 0;
     uint32_t acc_phase = 0;
     int g = g_begin, kb = kb_begin, left = n_units;
@@ -313,21 +348,33 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
           named_bar_sync(1, 128);
           finish = *s_last != 0;
           if (finish) {
-            // Sum the partials in contributor order; every load is issued before
-            // the first add of a contributor's slot.
+            // Sum the partials in contributor order (this CTA's own from its
+            // registers, the same values its slot would hold); every load of a
+            // slot is issued before the first add of it.
             const float* base = p.partials + static_cast<long long>(g) * p.maxc * SK_SLOT + q * 32 + lane;
+            float own[SK_TPU][SK_MN];
 #pragma unroll
             for (int j = 0; j < SK_TPU; ++j)
 #pragma unroll
-              for (int m = 0; m < SK_MN; ++m) v[j][m] = 0.0f;
+              for (int m = 0; m < SK_MN; ++m) {
+                own[j][m] = m < p.M ? v[j][m] : 0.0f;
+                v[j][m] = 0.0f;
+              }
             for (int jj = 0; jj < ncontrib; ++jj) {
               const float* sl = base + static_cast<long long>(jj) * SK_SLOT;
               float t[SK_TPU][SK_MN];
+              if (jj == jc) {
 #pragma unroll
-              for (int j = 0; j < SK_TPU; ++j)
+                for (int j = 0; j < SK_TPU; ++j)
 #pragma unroll
-                for (int m = 0; m < SK_MN; ++m)
-                  t[j][m] = m < p.M ? __ldcg(sl + (j * SK_MN + m) * SK_BN) : 0.0f;
+                  for (int m = 0; m < SK_MN; ++m) t[j][m] = own[j][m];
+              } else {
+#pragma unroll
+                for (int j = 0; j < SK_TPU; ++j)
+#pragma unroll
+                  for (int m = 0; m < SK_MN; ++m)
+                    t[j][m] = m < p.M ? __ldcg(sl + (j * SK_MN + m) * SK_BN) : 0.0f;
+              }
 #pragma unroll
               for (int j = 0; j < SK_TPU; ++j)
 #pragma unroll
@@ -458,11 +505,27 @@ int launch_skinny_gemm(const ojx_gemm_desc& d, cudaStream_t s, const Dests* dest
   if ((st = make_tmap_2d_sw128(&tx, tdt, 2, d.a, p.K, p.M, d.lda * 2, 64, SK_MN))) return st;
   const EpiParams ep = make_epi(d, dests);
   const bool bf = d.dtype_a == OJX_BF16;
+  // Programmatic stream serialization on eager launches (captured launches keep
+  // plain stream order): the grid may start while the previous kernel on the
+  // stream finishes, and holds every dependent access until griddepcontrol.wait.
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (s && cudaStreamIsCapturing(s, &cs) != cudaSuccess) cs = cudaStreamCaptureStatusActive;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = cs == cudaStreamCaptureStatusNone ? 1 : 0;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(p.G);
+  cfg.blockDim = dim3(SK_THREADS);
+  cfg.dynamicSmemBytes = SK_SMEM;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   auto launch = [&](auto kern) {
     int r = ensure_smem_attr(reinterpret_cast<const void*>(kern), SK_SMEM);
     if (r) return r;
-    kern<<<p.G, SK_THREADS, SK_SMEM, s>>>(tw, tx, ep, p);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tw, tx, ep, p);
     g_launches.fetch_add(1);
+    if (e != cudaSuccess) return cuda_status(e, "skinny_gemm launch");
     return cuda_status(cudaGetLastError(), "skinny_gemm launch");
   };
   if (bf) return w_mn ? launch(skinny_gemm_kernel<1, 1>) : launch(skinny_gemm_kernel<1, 0>);

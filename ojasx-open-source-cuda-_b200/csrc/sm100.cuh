@@ -96,6 +96,32 @@ __device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity, u
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
+// Fetch a 2-D tile into L2 only (no shared memory, no completion signal).  A
+// prefetch is a hint: reads issued later still observe every write to the tile.
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int32_t c0, int32_t c1) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1)
+               : "memory");
+}
+
+// Load with acquire semantics at GPU scope: later reads of this thread (and of
+// threads that synchronise with it afterwards) see what the releasing writer saw.
+__device__ __forceinline__ unsigned long long ld_acquire_gpu_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// ── programmatic dependent launch ───────────────────────────────────────────
+// Block until the grids this one depends on (the previous kernel on the stream,
+// when it was launched with programmatic stream serialization) have completed and
+// their memory writes are visible.  Returns at once without such a dependency.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Allow the next kernel on the stream to begin launching before this grid ends.
+__device__ __forceinline__ void grid_dep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 // 2-D tiled load into this CTA's shared memory; completion is signalled on `bar`
 // through complete_tx.  c0 is the innermost coordinate (elements).
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
