@@ -26,14 +26,19 @@
 // every time) then starts from zero as well.
 //
 // Back-to-back decode launches (one per layer) overlap through programmatic
-// dependent launch: each grid lets the next one start as soon as it is resident,
-// and the next grid's CTAs, placed as this grid's CTAs exit, set up and prefetch
-// their first SK_PREFETCH units of W into L2 before griddepcontrol.wait.  Every
-// other global access (X, the epilogue operand, C, the scratch) comes after that
-// wait, so it sees all of the previous kernel's writes.  HBM then keeps streaming
-// across the previous launch's split-K tail instead of idling through it.
+// dependent launch.  The kernel is sized for two CTAs per SM (3-stage ring,
+// 8-row epilogue staging: ~111 KB of shared memory), and each CTA lets the next
+// launch in once it has issued its last W load.  The next grid's CTAs then take
+// the second slot on every SM, set up, and (when the host has established that
+// the previous launch does not write W) load the W tiles of their first units
+// into their ring while this grid drains and runs its split-K tail; only then do
+// they pass griddepcontrol.wait.  Every other global access (X, the epilogue
+// operand, C, the scratch) comes after that wait, so it sees all of the previous
+// kernel's writes.
 #include <cuda_runtime.h>
 #include <algorithm>
+#include <mutex>
+#include <unordered_map>
 #include "sm100.cuh"
 #include "epilogue.cuh"
 #include "internal.h"
@@ -45,17 +50,21 @@ constexpr int SK_BN = 128;   // columns of C per tile (MMA M)
 constexpr int SK_TPU = 2;    // tiles per unit
 constexpr int SK_MN = 16;    // padded rows of X (MMA N)
 constexpr int SK_BK = 64;    // k per unit (one 128-byte swizzle row of bf16)
-constexpr int SK_STAGES = 6;
+constexpr int SK_STAGES = 3;
 constexpr int SK_THREADS = 192;
 constexpr int SK_W_BYTES = SK_TPU * SK_BN * 128;
 constexpr int SK_X_BYTES = SK_MN * 128;
 constexpr int SK_STAGE_BYTES = SK_W_BYTES + SK_X_BYTES;
 constexpr int SK_NBUF = 4;  // TMEM accumulator buffers (segments in flight)
-constexpr int SK_PREFETCH = 8;  // units of W fetched into L2 before the dependency wait
 constexpr uint32_t SK_TMEM_COLS = SK_NBUF * SK_TPU * SK_MN;
 constexpr int SK_SLOT = SK_TPU * SK_MN * SK_BN;  // floats per partial slot
-constexpr int SK_EPI_BYTES = SK_TPU * SK_MN * SK_BN * 4;  // finished block, fp32
+constexpr int SK_EPI_ROWS = 8;  // rows of a finished group staged at a time
+constexpr int SK_EPI_BYTES = SK_TPU * SK_EPI_ROWS * SK_BN * 4;  // staging, fp32
 constexpr int SK_SMEM = SK_STAGES * SK_STAGE_BYTES + SK_EPI_BYTES + 512 + 1024;
+// Two CTAs per SM (228 KB of shared memory, 1 KB reserved per CTA): the next
+// launch's CTAs become resident beside this launch's while it drains.
+static_assert(2 * (SK_SMEM + 1024) <= 228 * 1024, "two skinny CTAs must fit on one SM");
+static_assert(SK_MN == 2 * SK_EPI_ROWS, "the finish stages the rows in two passes");
 static_assert(SK_TPU * SK_BN == 256, "the finish maps 32 threads x 8 columns onto one row of a group");
 static_assert(SK_STAGE_BYTES % 1024 == 0, "stage alignment");
 static_assert(SK_TMEM_COLS >= 32 && (SK_TMEM_COLS & (SK_TMEM_COLS - 1)) == 0, "TMEM alloc size");
@@ -71,6 +80,8 @@ struct SkinnyParams {
   unsigned int epoch;
   uint64_t budget;
   int silence_producer;
+  int trigger_early;  // let the next launch in after the last W load is issued
+  int early_w;        // W of the first SK_STAGES units may be loaded before the dependency wait
 };
 
 __device__ __forceinline__ long long unit_begin(int c, const SkinnyParams& p) {
@@ -84,8 +95,19 @@ __device__ __forceinline__ int cta_of_unit(long long u, const SkinnyParams& p) {
   return c;
 }
 
+// A CTA visits its units [ub, ue) starting with the head of the last group it
+// touches, when that head is only part of the group (its other k blocks belong
+// to later CTAs), then wraps around to ub.  Its partial for that group is then
+// written early, and the one segment this CTA ends its stream with is the tail
+// of its first group, which the CTAs before it began early: at the end of the
+// stream each CTA has at most one split-K arrival (and one finish) left to do.
+__device__ __forceinline__ long long first_unit(long long ub, long long ue, int KB) {
+  const long long hs = (ue - 1) / KB * KB;
+  return (hs > ub && ue % KB != 0) ? hs : ub;
+}
+
 template <int FMT, int W_MN>
-__global__ void __launch_bounds__(SK_THREADS, 1)
+__global__ void __launch_bounds__(SK_THREADS, 2)
     skinny_gemm_kernel(const __grid_constant__ CUtensorMap tmW,
                        const __grid_constant__ CUtensorMap tmX, const EpiParams ep,
                        const SkinnyParams p) {
@@ -134,47 +156,35 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *s_tmem;
-  // Every CTA of this grid is resident: the next launch may begin.  Its CTAs only
-  // find room on an SM once this grid's CTA there has exited.
-  grid_dep_launch_dependents();
 
   const long long ub = unit_begin(blockIdx.x, p);
   const long long ue = unit_begin(blockIdx.x + 1, p);
   const int g_begin = static_cast<int>(ub / p.KB);
   const int kb_begin = static_cast<int>(ub - static_cast<long long>(g_begin) * p.KB);
   const int n_units = static_cast<int>(ue - ub);
+  const long long u_first = first_unit(ub, ue, p.KB);
+  const int g_first = static_cast<int>(u_first / p.KB);
+  const int kb_first = static_cast<int>(u_first - static_cast<long long>(g_first) * p.KB);
+  // Step (u, g, kb) by n units in the visiting order (n never crosses ue).
+  auto advance = [&](long long& u, int& g, int& kb, int n) {
+    u += n;
+    if (u == ue) {
+      u = ub;
+      g = g_begin;
+      kb = kb_begin;
+    } else {
+      kb += n;
+      if (kb == p.KB) {
+        kb = 0;
+        ++g;
+      }
+    }
+  };
 
   if (warp == 0) {
     // ── TMA producer ────────────────────────────────────────────────────
     if (lane == 0 && !p.silence_producer) {
-      {  // W tiles of the first units into L2 while the previous grid finishes
-        int g = g_begin, kb = kb_begin;
-        const int npf = min(n_units, SK_PREFETCH);
-        for (int i = 0; i < npf; ++i) {
-          const int n0 = g * (SK_TPU * SK_BN), k0 = kb * SK_BK;
-#pragma unroll
-          for (int j = 0; j < SK_TPU; ++j) {
-            if (W_MN) {
-              tma_prefetch_l2_2d(&tmW, n0 + j * SK_BN, k0);
-              tma_prefetch_l2_2d(&tmW, n0 + j * SK_BN + 64, k0);
-            } else {
-              tma_prefetch_l2_2d(&tmW, k0, n0 + j * SK_BN);
-            }
-          }
-          if (++kb == p.KB) {
-            kb = 0;
-            ++g;
-          }
-        }
-      }
-      grid_dep_wait();
-      int stage = 0, g = g_begin, kb = kb_begin;
-      uint32_t phase = 0, issued = 0, issued_parity = 0;
-      for (int i = 0; i < n_units; ++i) {
-        if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.budget, s_abort)) break;
-        const uint32_t fb = full_bar(stage);
-        mbar_arrive_expect_tx(fb, SK_STAGE_BYTES);
-        const uint32_t sW = sbase + stage * SK_STAGE_BYTES;
+      auto load_w = [&](uint32_t sW, uint32_t fb, int g, int kb) {
         const int n0 = g * (SK_TPU * SK_BN), k0 = kb * SK_BK;
 #pragma unroll
         for (int j = 0; j < SK_TPU; ++j) {
@@ -185,18 +195,53 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
             tma_load_2d(sW + j * (SK_BN * 128), &tmW, fb, k0, n0 + j * SK_BN);
           }
         }
-        tma_load_2d(sW + SK_W_BYTES, &tmX, fb, k0, 0);
+      };
+      // Before the dependency wait, while the previous grid drains: the W tiles
+      // of the first n_early units go straight into the (empty) ring when the
+      // host has established that the previous launch on this stream does not
+      // write W (p.early_w).  X, which that launch usually wrote, is loaded after
+      // the wait.
+      const int n_early = p.early_w ? min(n_units, SK_STAGES) : 0;
+      {
+        long long u = u_first;
+        int g = g_first, kb = kb_first;
+        for (int i = 0; i < n_early; ++i) {
+          mbar_arrive_expect_tx(full_bar(i), SK_STAGE_BYTES);
+          load_w(sbase + i * SK_STAGE_BYTES, full_bar(i), g, kb);
+          advance(u, g, kb, 1);
+        }
+      }
+      grid_dep_wait();
+      int stage = 0, g = g_first, kb = kb_first;
+      long long u = u_first;
+      uint32_t phase = 0, issued = 0, issued_parity = 0;
+      for (int i = 0; i < n_early; ++i) {  // X of the units whose W is already on its way
+        tma_load_2d(sbase + i * SK_STAGE_BYTES + SK_W_BYTES, &tmX, full_bar(i), kb * SK_BK, 0);
+        issued |= 1u << i;
+        advance(u, g, kb, 1);
+      }
+      stage = n_early % SK_STAGES;
+      phase = n_early == SK_STAGES ? 1u : 0u;
+      for (int i = n_early; i < n_units; ++i) {
+        if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.budget, s_abort)) break;
+        const uint32_t fb = full_bar(stage);
+        mbar_arrive_expect_tx(fb, SK_STAGE_BYTES);
+        const uint32_t sW = sbase + stage * SK_STAGE_BYTES;
+        load_w(sW, fb, g, kb);
+        tma_load_2d(sW + SK_W_BYTES, &tmX, fb, kb * SK_BK, 0);
         issued |= 1u << stage;
         issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
         if (++stage == SK_STAGES) {
           stage = 0;
           phase ^= 1u;
         }
-        if (++kb == p.KB) {
-          kb = 0;
-          ++g;
-        }
+        advance(u, g, kb, 1);
       }
+      // Every W load of this CTA is issued: the next launch may begin.  Its CTAs
+      // take the second slot on each SM and start on their first units while this
+      // grid drains its ring and runs its split-K tail.  (The first execution in a
+      // CTA counts; a CTA that exits without it counts too.)
+      if (p.trigger_early) grid_dep_launch_dependents();
       for (int s = 0; s < SK_STAGES; ++s)
         if ((issued >> s) & 1u) mbar_wait_drain(full_bar(s), (issued_parity >> s) & 1u, p.budget);
     }
@@ -205,11 +250,12 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
     if (lane == 0) {
       grid_dep_wait();  // the bounded waits below start once the inputs are final
       constexpr uint32_t IDESC = make_idesc(FMT, W_MN, 0, SK_BN, SK_MN);
-      int stage = 0, acc = 0, kb = kb_begin;
+      int stage = 0, acc = 0, g = g_first, kb = kb_first;
+      long long u = u_first;
       uint32_t phase = 0, acc_phase = 0;
       bool seg_start = true;
       for (int i = 0; i < n_units; ++i) {
-        const bool seg_end = (i + 1 == n_units) || (kb + 1 == p.KB);
+        const bool seg_end = (i + 1 == n_units) || (kb + 1 == p.KB) || (u + 1 == ue);
         if (seg_start) {
           if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, p.budget, s_abort)) break;
           tc_fence_after();
@@ -244,7 +290,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
             acc_phase ^= 1u;
           }
         }
-        if (++kb == p.KB) kb = 0;
+        advance(u, g, kb, 1);
       }
       mma_commit(done_bar);
       mbar_wait_drain(done_bar, 0, p.budget);
@@ -257,7 +303,8 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
     grid_dep_wait();  // the operand, C and the scratch may belong to the previous kernel
     int acc = 0;
     uint32_t acc_phase = 0;
-    int g = g_begin, kb = kb_begin, left = n_units;
+    int g = g_first, kb = kb_first, left = n_units;
+    long long u = u_first;
     // Pass 0 runs the finishing code once on zeros with its stores disabled, while
     // the accumulators are still far from ready: the tail's first real finish then
     // finds that code in the instruction caches instead of fetching it from memory
@@ -269,6 +316,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
       if (!warm && left <= 0) break;
       float v[SK_TPU][SK_MN];
       bool finish = true;
+      int seg_units = 0;
       // In the finish below, thread etid owns the 8 columns fc .. fc+7 of the
       // group (fc = 8 * (etid % 32)) in rows etid / 32, + 4, + 8, + 12.  Their
       // row operand (bias) is loaded here, before the accumulator is ready, so
@@ -287,7 +335,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
 #pragma unroll
           for (int m = 0; m < SK_MN; ++m) v[j][m] = 0.0f;
       } else {
-        const int seg_units = min(left, p.KB - kb);
+        seg_units = static_cast<int>(min(static_cast<long long>(min(left, p.KB - kb)), ue - u));
         const bool whole_from_start = (kb == 0);
         left -= seg_units;
         // The four epilogue warps meet at named barriers below, so they must agree
@@ -327,9 +375,12 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
               if (m < p.M) slot[(j * SK_MN + m) * SK_BN] = v[j][m];
           named_bar_sync(1, 128);
           if (etid == 0) {
-            __threadfence();
+            fence_acq_rel_gpu();  // with the barrier above: releases every thread's slot
             unsigned long long* ctr = p.counters + g;
-            unsigned long long old = *reinterpret_cast<volatile unsigned long long*>(ctr);
+            // First guess: this CTA is the last to arrive (the case on the tail's
+            // critical path), so the last arriver needs a single atomic.
+            unsigned long long old =
+                (static_cast<unsigned long long>(p.epoch) << 32) | static_cast<unsigned int>(ncontrib - 1);
             unsigned int count;
             while (true) {  // ends as soon as the CAS succeeds
               const unsigned int e = static_cast<unsigned int>(old >> 32);
@@ -342,93 +393,112 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
             *s_last = (count == static_cast<unsigned int>(ncontrib)) ? 1 : 0;
             if (*s_last) {
               *ctr = 0ull;  // every contributor of this group has arrived
-              __threadfence();
+              fence_acq_rel_gpu();  // acquire: the other slots are read after this
             }
           }
           named_bar_sync(1, 128);
           finish = *s_last != 0;
           if (finish) {
             // Sum the partials in contributor order (this CTA's own from its
-            // registers, the same values its slot would hold); every load of a
-            // slot is issued before the first add of it.
+            // registers, the same values its slot holds), four rows and four
+            // contributors at a time: every load of a batch is issued before its
+            // first add, so M <= 4 with up to four contributors costs one L2
+            // round trip.
             const float* base = p.partials + static_cast<long long>(g) * p.maxc * SK_SLOT + q * 32 + lane;
-            float own[SK_TPU][SK_MN];
 #pragma unroll
-            for (int j = 0; j < SK_TPU; ++j)
+            for (int mc = 0; mc < SK_MN / 4; ++mc) {
+              if (4 * mc >= p.M) break;
+              float sum[SK_TPU][4];
 #pragma unroll
-              for (int m = 0; m < SK_MN; ++m) {
-                own[j][m] = m < p.M ? v[j][m] : 0.0f;
-                v[j][m] = 0.0f;
-              }
-            for (int jj = 0; jj < ncontrib; ++jj) {
-              const float* sl = base + static_cast<long long>(jj) * SK_SLOT;
-              float t[SK_TPU][SK_MN];
-              if (jj == jc) {
+              for (int j = 0; j < SK_TPU; ++j)
 #pragma unroll
-                for (int j = 0; j < SK_TPU; ++j)
+                for (int mm = 0; mm < 4; ++mm) sum[j][mm] = 0.0f;
+              for (int jj0 = 0; jj0 < ncontrib; jj0 += 4) {
+                float t[4][SK_TPU][4];
 #pragma unroll
-                  for (int m = 0; m < SK_MN; ++m) t[j][m] = own[j][m];
-              } else {
+                for (int bb = 0; bb < 4; ++bb) {
+                  const int jj = jj0 + bb;
+                  const float* sl = base + static_cast<long long>(jj) * SK_SLOT;
 #pragma unroll
-                for (int j = 0; j < SK_TPU; ++j)
+                  for (int j = 0; j < SK_TPU; ++j)
 #pragma unroll
-                  for (int m = 0; m < SK_MN; ++m)
-                    t[j][m] = m < p.M ? __ldcg(sl + (j * SK_MN + m) * SK_BN) : 0.0f;
+                    for (int mm = 0; mm < 4; ++mm) {
+                      const int m = 4 * mc + mm;
+                      t[bb][j][mm] = (jj < ncontrib && jj != jc && m < p.M)
+                                         ? __ldcg(sl + (j * SK_MN + m) * SK_BN)
+                                         : v[j][m];
+                    }
+                }
+#pragma unroll
+                for (int bb = 0; bb < 4; ++bb)
+                  if (jj0 + bb < ncontrib)
+#pragma unroll
+                    for (int j = 0; j < SK_TPU; ++j)
+#pragma unroll
+                      for (int mm = 0; mm < 4; ++mm) sum[j][mm] += t[bb][j][mm];
               }
 #pragma unroll
               for (int j = 0; j < SK_TPU; ++j)
 #pragma unroll
-                for (int m = 0; m < SK_MN; ++m) v[j][m] += t[j][m];
+                for (int mm = 0; mm < 4; ++mm) v[j][4 * mc + mm] = sum[j][mm];
             }
           }
           named_bar_sync(1, 128);  // s_last may be rewritten by the next segment
         }
       }
       if (finish) {
-        // Stage the finished M x 256 block in shared memory, then each thread
-        // runs the 8-wide epilogue on its 8 columns of every fourth row and
-        // writes them with one 16-byte store per destination (a warp covers a
-        // whole 256-column row: 512 contiguous bytes).
-#pragma unroll
-        for (int j = 0; j < SK_TPU; ++j)
-#pragma unroll
-          for (int m = 0; m < SK_MN; ++m)
-            if (m < p.M) st_shared_f32(epi_u32 + 4u * ((j * SK_MN + m) * SK_BN + q * 32 + lane), v[j][m]);
-        named_bar_sync(1, 128);
-        if (fvalid > 0) {
+        // Stage SK_EPI_ROWS rows of the finished M x 256 block at a time in shared
+        // memory, then each thread runs the 8-wide epilogue on its 8 columns of
+        // every fourth staged row and writes them with one 16-byte store per
+        // destination (a warp covers a whole 256-column row: 512 contiguous
+        // bytes).  The second pass (rows 8..15) selects its registers with
+        // compile-time indices, so v stays in registers.
 #pragma unroll 1
-          for (int m = etid >> 5; m < p.M; m += 4) {
-            float y[8], x[8];
-            const uint32_t sa = epi_u32 + 4u * (((fc >> 7) * SK_MN + m) * SK_BN + (fc & 127));
+        for (int r0 = 0; r0 < p.M; r0 += SK_EPI_ROWS) {
 #pragma unroll
-            for (int k = 0; k < 8; ++k) y[k] = ld_shared_f32(sa + 4u * k);
-            if (ep.operand_kind == OJX_OPERAND_FULL)
-              load8(ep.operand, ep.dtype_operand, static_cast<int64_t>(m) * ep.ld_operand + fn,
-                    fvalid, x);
-            else
+          for (int j = 0; j < SK_TPU; ++j)
 #pragma unroll
-              for (int k = 0; k < 8; ++k) x[k] = row_op[k];
-            if (ep.operand_kind != OJX_OPERAND_NONE)
-              binary_n<8>(ep.binary_op, ep.operand_is_lhs != 0, y, x);
-            for (int i = 0; i < ep.n_unary; ++i) unary_n_half<8>(unary_at(ep.unary_packed, i), y);
-            if (!warm) {
+            for (int mm = 0; mm < SK_EPI_ROWS; ++mm)
+              if (r0 + mm < p.M)
+                st_shared_f32(epi_u32 + 4u * ((j * SK_EPI_ROWS + mm) * SK_BN + q * 32 + lane),
+                              r0 ? v[j][SK_EPI_ROWS + mm] : v[j][mm]);
+          named_bar_sync(1, 128);
+          if (fvalid > 0) {
+            const int r1 = min(p.M, r0 + SK_EPI_ROWS);
+#pragma unroll 1
+            for (int m = r0 + (etid >> 5); m < r1; m += 4) {
+              float y[8], x[8];
+              const uint32_t sa =
+                  epi_u32 + 4u * (((fc >> 7) * SK_EPI_ROWS + (m - r0)) * SK_BN + (fc & 127));
 #pragma unroll
-              for (int di = 0; di < OJX_MAX_PEERS; ++di) {
-                if (di >= ep.n_dst) break;
-                store8(ep.dst[di], ep.dtype_c, static_cast<int64_t>(m) * ep.ldc + ep.col_offset + fn,
-                       fvalid, y);
+              for (int k = 0; k < 8; ++k) y[k] = ld_shared_f32(sa + 4u * k);
+              if (ep.operand_kind == OJX_OPERAND_FULL)
+                load8(ep.operand, ep.dtype_operand, static_cast<int64_t>(m) * ep.ld_operand + fn,
+                      fvalid, x);
+              else
+#pragma unroll
+                for (int k = 0; k < 8; ++k) x[k] = row_op[k];
+              if (ep.operand_kind != OJX_OPERAND_NONE)
+                binary_n<8>(ep.binary_op, ep.operand_is_lhs != 0, y, x);
+              for (int i = 0; i < ep.n_unary; ++i) unary_n_half<8>(unary_at(ep.unary_packed, i), y);
+              if (!warm) {
+#pragma unroll
+                for (int di = 0; di < OJX_MAX_PEERS; ++di) {
+                  if (di >= ep.n_dst) break;
+                  store8(ep.dst[di], ep.dtype_c,
+                         static_cast<int64_t>(m) * ep.ldc + ep.col_offset + fn, fvalid, y);
+                }
               }
             }
           }
+          named_bar_sync(1, 128);  // the staging block is rewritten by the next pass
         }
-        named_bar_sync(1, 128);  // the staging block is rewritten by the next finish
       }
       if (warm) {
         warm = 0;
         continue;
       }
-      kb = 0;
-      ++g;
+      advance(u, g, kb, seg_units);
     }
     if (ep.n_dst > 1) __threadfence_system();  // peer stores visible before completion
   }
@@ -470,6 +540,19 @@ static int skinny_max_contrib(int n_groups, int KB, long long U, int G) {
   return mx;
 }
 
+// Byte ranges written by the last eager skinny launch on each stream.  The next
+// eager launch on that stream may start before it completes (programmatic
+// dependent launch); it loads W ahead of its dependency wait only when W lies
+// outside these ranges.  (A kernel of any other kind in between completes before
+// the next launch starts, so only the last skinny launch can still be writing.)
+struct SkinnyOut {
+  int n = 0;
+  uintptr_t lo[OJX_MAX_PEERS], hi[OJX_MAX_PEERS];
+};
+static std::mutex g_skinny_out_mu;
+static std::unordered_map<cudaStream_t, SkinnyOut>* g_skinny_out =
+    new std::unordered_map<cudaStream_t, SkinnyOut>();
+
 int launch_skinny_gemm(const ojx_gemm_desc& d, cudaStream_t s, const Dests* dests) {
   SkinnyParams p{};
   p.M = static_cast<int>(d.M);
@@ -506,10 +589,33 @@ int launch_skinny_gemm(const ojx_gemm_desc& d, cudaStream_t s, const Dests* dest
   const EpiParams ep = make_epi(d, dests);
   const bool bf = d.dtype_a == OJX_BF16;
   // Programmatic stream serialization on eager launches (captured launches keep
-  // plain stream order): the grid may start while the previous kernel on the
-  // stream finishes, and holds every dependent access until griddepcontrol.wait.
+  // plain stream order and never let the next kernel in early): the grid may
+  // start while the previous kernel on the stream finishes, and holds every
+  // dependent access until griddepcontrol.wait.
   cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
   if (s && cudaStreamIsCapturing(s, &cs) != cudaSuccess) cs = cudaStreamCaptureStatusActive;
+  const bool eager = cs == cudaStreamCaptureStatusNone;
+  p.trigger_early = eager ? 1 : 0;
+  {
+    const uintptr_t w_lo = reinterpret_cast<uintptr_t>(d.b);
+    const uintptr_t w_hi =
+        w_lo + 2u * static_cast<uintptr_t>(w_mn ? (d.K - 1) * d.ldb + d.N : (d.N - 1) * d.ldb + d.K);
+    const int esz_c = d.dtype_c == OJX_F32 ? 4 : 2;
+    const uintptr_t c_len =
+        static_cast<uintptr_t>(esz_c) * static_cast<uintptr_t>((d.M - 1) * ep.ldc + ep.col_offset + d.N);
+    std::lock_guard<std::mutex> lk(g_skinny_out_mu);
+    SkinnyOut& last = (*g_skinny_out)[s];
+    bool overlap = false;
+    for (int i = 0; i < last.n; ++i) overlap |= w_lo < last.hi[i] && last.lo[i] < w_hi;
+    p.early_w = eager && !overlap ? 1 : 0;
+    if (eager) {
+      last.n = ep.n_dst;
+      for (int i = 0; i < ep.n_dst; ++i) {
+        last.lo[i] = reinterpret_cast<uintptr_t>(ep.dst[i]);
+        last.hi[i] = last.lo[i] + c_len;
+      }
+    }
+  }
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = cs == cudaStreamCaptureStatusNone ? 1 : 0;

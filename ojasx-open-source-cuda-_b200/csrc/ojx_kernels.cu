@@ -59,10 +59,15 @@ static int noalloc_setup(void** out) {
                               reinterpret_cast<const void*>(skinny_gemm_kernel<1, 0>),
                               reinterpret_cast<const void*>(skinny_gemm_kernel<0, 1>),
                               reinterpret_cast<const void*>(skinny_gemm_kernel<0, 0>)};
-    for (const void* k : kernels)
+    for (const void* k : kernels) {
       if ((st = cuda_status(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SK_SMEM),
                             "cudaFuncSetAttribute")))
         return st;
+      if ((st = cuda_status(cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                                 cudaSharedmemCarveoutMaxShared),
+                            "cudaFuncSetAttribute(carveout)")))
+        return st;
+    }
     g_noalloc_ptr[dev] = p;
   }
   *out = g_noalloc_ptr[dev];
@@ -131,6 +136,8 @@ extern "C" int ojx_gemm_skinny_noalloc(const ojx_gemm_desc* in, ojx_stream strea
   if (p.epoch == 0) p.epoch = g_skinny_epoch.fetch_add(1);
   p.budget = g_wait_budget.load();
   p.silence_producer = 0;
+  p.trigger_early = 0;  // plain launch: the next kernel starts after this one completes
+  p.early_w = 0;
 
   const CUtensorMapDataType tdt =
       d.dtype_a == OJX_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;

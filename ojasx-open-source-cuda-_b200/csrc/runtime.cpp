@@ -59,6 +59,11 @@ int ensure_smem_attr(const void* kernel, int bytes) {
   if (it != done->end() && it->second >= bytes) return OJX_OK;
   int st = cuda_status(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes),
                        "cudaFuncSetAttribute");
+  // Whole shared-memory carveout, so kernels sized for two CTAs per SM get both.
+  if (!st)
+    st = cuda_status(cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                          cudaSharedmemCarveoutMaxShared),
+                     "cudaFuncSetAttribute(carveout)");
   if (!st) (*done)[key] = bytes;
   return st;
 }

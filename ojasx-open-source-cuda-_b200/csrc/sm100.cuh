@@ -113,6 +113,11 @@ __device__ __forceinline__ unsigned long long ld_acquire_gpu_u64(const unsigned 
   return v;
 }
 
+// Release/acquire fence at GPU scope (lighter than __threadfence's sequentially
+// consistent fence): before a signalling atomic it releases the writes that this
+// thread observed, after an observing atomic it acquires the writes it announced.
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+
 // ── programmatic dependent launch ───────────────────────────────────────────
 // Block until the grids this one depends on (the previous kernel on the stream,
 // when it was launched with programmatic stream serialization) have completed and
