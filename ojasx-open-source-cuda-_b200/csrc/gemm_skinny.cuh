@@ -116,7 +116,7 @@ __global__ void __launch_bounds__(SK_THREADS, 2)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const uint32_t epi_u32 = smem_u32(smem + SK_STAGES * SK_STAGE_BYTES);  // finished block
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SK_STAGES * SK_STAGE_BYTES + SK_EPI_BYTES);
-  constexpr int NB = 2 * SK_STAGES + 2 * SK_NBUF + 1;  // full, empty, tfull, tempty, done
+  constexpr int NB = 2 * SK_STAGES + 2 * SK_NBUF + 2;  // full, empty, tfull, tempty, done, red
   volatile int* s_abort = reinterpret_cast<volatile int*>(bars + NB);
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + NB + 1);
   volatile int* s_last = reinterpret_cast<volatile int*>(bars + NB + 2);
@@ -130,6 +130,7 @@ __global__ void __launch_bounds__(SK_THREADS, 2)
   auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * SK_STAGES + a); };
   auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * SK_STAGES + SK_NBUF + a); };
   const uint32_t done_bar = bar0 + 8u * (2 * SK_STAGES + 2 * SK_NBUF);
+  const uint32_t red_bar = done_bar + 8u;  // partial slots copied in for the last finish
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < SK_STAGES; ++s) {
@@ -141,6 +142,7 @@ __global__ void __launch_bounds__(SK_THREADS, 2)
       mbar_init(tempty_bar(a), 4);
     }
     mbar_init(done_bar, 1);
+    mbar_init(red_bar, 1);
     *s_abort = 0;
     fence_mbar_init();
   }
@@ -336,8 +338,22 @@ __global__ void __launch_bounds__(SK_THREADS, 2)
           for (int m = 0; m < SK_MN; ++m) v[j][m] = 0.0f;
       } else {
         seg_units = static_cast<int>(min(static_cast<long long>(min(left, p.KB - kb)), ue - u));
-        const bool whole_from_start = (kb == 0);
+        const bool whole = kb == 0 && seg_units == p.KB;
         left -= seg_units;
+        // The group's contributors (64-bit divisions) are worked out while the
+        // accumulator is still being computed.
+        int c_first = blockIdx.x, ncontrib = 1;
+        if (!whole) {
+          c_first = cta_of_unit(static_cast<long long>(g) * p.KB, p);
+          const int c_last = cta_of_unit(min(static_cast<long long>(g + 1) * p.KB, p.U) - 1, p);
+          ncontrib = c_last - c_first + 1;
+        }
+        const int jc = blockIdx.x - c_first;
+        // With more than 4 rows, the last finish of the CTA (its ring is idle by
+        // then: every MMA has completed) bulk-copies the other contributors' slots
+        // into the ring, one round trip instead of one per 4 rows; with up to 4
+        // rows, loads into registers are already a single round trip and faster.
+        const bool staged = left <= 0 && p.M > 4 && ncontrib * p.M * 1024 <= SK_STAGES * SK_STAGE_BYTES;
         // The four epilogue warps meet at named barriers below, so they must agree
         // on whether to go on: any warp that failed its wait stops all four.
         const bool waited = mbar_wait(tfull_bar(acc), acc_phase, p.budget, s_abort);
@@ -360,12 +376,7 @@ __global__ void __launch_bounds__(SK_THREADS, 2)
         for (int j = 0; j < SK_TPU; ++j)
 #pragma unroll
           for (int m = 0; m < SK_MN; ++m) v[j][m] = __uint_as_float(r[j][m]);
-        const bool whole = whole_from_start && seg_units == p.KB;
         if (!whole) {
-          const int c_first = cta_of_unit(static_cast<long long>(g) * p.KB, p);
-          const int c_last = cta_of_unit(min(static_cast<long long>(g + 1) * p.KB, p.U) - 1, p);
-          const int ncontrib = c_last - c_first + 1;
-          const int jc = blockIdx.x - c_first;
           float* slot = p.partials + (static_cast<long long>(g) * p.maxc + jc) * SK_SLOT +
                         q * 32 + lane;
 #pragma unroll
@@ -392,13 +403,56 @@ __global__ void __launch_bounds__(SK_THREADS, 2)
             }
             *s_last = (count == static_cast<unsigned int>(ncontrib)) ? 1 : 0;
             if (*s_last) {
-              *ctr = 0ull;  // every contributor of this group has arrived
               fence_acq_rel_gpu();  // acquire: the other slots are read after this
+              *ctr = 0ull;          // every contributor of this group has arrived
+              if (staged) {
+                fence_proxy_async_all();  // the slots are read through the async proxy
+                mbar_arrive_expect_tx(red_bar, static_cast<uint32_t>((ncontrib - 1) * SK_TPU * p.M * 512));
+                const float* gb = p.partials + static_cast<long long>(g) * p.maxc * SK_SLOT;
+                for (int jj = 0; jj < ncontrib; ++jj) {
+                  if (jj == jc) continue;
+#pragma unroll
+                  for (int j = 0; j < SK_TPU; ++j)
+                    bulk_load_g2s(sbase + static_cast<uint32_t>(((jj * SK_TPU + j) * p.M) * 512),
+                                  gb + static_cast<long long>(jj) * SK_SLOT + j * SK_MN * SK_BN,
+                                  static_cast<uint32_t>(p.M * 512), red_bar);
+                }
+              }
             }
           }
           named_bar_sync(1, 128);
           finish = *s_last != 0;
-          if (finish) {
+          if (finish && staged) {
+            // Part (jj, j) = rows 0..M-1 of tile j of contributor jj's slot lands at
+            // (jj * 2 + j) * M * 512 in the ring (bulk copies issued above by the
+            // thread that took the last arrival); this thread's own values go to
+            // their place too, then it sums its column over the contributors in
+            // contributor order (the same order, and so the same result, as below).
+            const uint32_t col4 = 4u * static_cast<uint32_t>(q * 32 + lane);
+#pragma unroll
+            for (int j = 0; j < SK_TPU; ++j)
+#pragma unroll
+              for (int m = 0; m < SK_MN; ++m)
+                if (m < p.M)
+                  st_shared_f32(sbase + static_cast<uint32_t>(((jc * SK_TPU + j) * p.M + m) * 512) + col4,
+                                v[j][m]);
+            const bool ok = mbar_wait(red_bar, 0, p.budget, s_abort);
+            if (named_bar_red_or(1, 128, !ok)) {
+              if (etid == 0) mbar_wait_drain(red_bar, 0, p.budget);  // copies still in flight
+              break;
+            }
+#pragma unroll
+            for (int j = 0; j < SK_TPU; ++j)
+#pragma unroll
+              for (int m = 0; m < SK_MN; ++m) v[j][m] = 0.0f;
+            for (int jj = 0; jj < ncontrib; ++jj)
+#pragma unroll
+              for (int j = 0; j < SK_TPU; ++j)
+#pragma unroll
+                for (int m = 0; m < SK_MN; ++m)
+                  if (m < p.M)
+                    v[j][m] += ld_shared_f32(sbase + static_cast<uint32_t>(((jj * SK_TPU + j) * p.M + m) * 512) + col4);
+          } else if (finish) {
             // Sum the partials in contributor order (this CTA's own from its
             // registers, the same values its slot holds), four rows and four
             // contributors at a time: every load of a batch is issued before its

@@ -118,6 +118,19 @@ __device__ __forceinline__ unsigned long long ld_acquire_gpu_u64(const unsigned 
 // thread observed, after an observing atomic it acquires the writes it announced.
 __device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
 
+// Untiled bulk copy of `bytes` (a multiple of 16; both addresses 16-byte aligned)
+// from global memory into this CTA's shared memory, completing on `bar` through
+// complete_tx.  No multicast.
+__device__ __forceinline__ void bulk_load_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   dst),
+               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
+               : "memory");
+}
+// Orders this thread's earlier generic-proxy accesses (and what it acquired)
+// before its later async-proxy (TMA) accesses, in every state space.
+__device__ __forceinline__ void fence_proxy_async_all() { asm volatile("fence.proxy.async;" ::: "memory"); }
+
 // ── programmatic dependent launch ───────────────────────────────────────────
 // Block until the grids this one depends on (the previous kernel on the stream,
 // when it was launched with programmatic stream serialization) have completed and
