@@ -79,6 +79,9 @@ bool flash_attn_supported(int dtype, int64_t D);
 int launch_flash_attn(const void* q, const void* k, const void* v, void* out, int dtype, int64_t BH,
                       int64_t M, int64_t N, int64_t nk, int64_t D, float scale, int causal,
                       cudaStream_t s);
+int launch_flash_attn2(const void* q, const void* k, const void* v, void* out, int dtype, int64_t BH,
+                      int64_t M, int64_t N, int64_t nk, int64_t D, float scale, int causal,
+                      cudaStream_t s);
 int launch_attn_softmax(const float* S, int64_t ld, int64_t rows, int M, int nk, float scale,
                         int causal, void* P, int dtype_p, cudaStream_t s);
 int launch_sum_columns(void* out, int dt_out, const void* in, int dt_in, int64_t rows, int64_t cols,

@@ -6,6 +6,7 @@
 #include "gemm_skinny.cuh"
 #include "attention.cuh"
 #include "flash_attn.cuh"
+#include "flash_attn2.cuh"
 #include <mutex>
 
 // ── decode GEMM for callers that cannot allocate device memory ───────────────

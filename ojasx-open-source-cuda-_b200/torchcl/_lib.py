@@ -30,6 +30,7 @@ FP32_AUTO, FP32_3XTF32, FP32_FFMA = 0, 1, 2
 FLAG_FORCE_SIMT, FLAG_NO_SKINNY, FLAG_FORCE_SKINNY = 0x1, 0x2, 0x4
 ROUTES = {0: "none", 1: "tc_f16", 2: "tc_3xtf32", 3: "skinny", 4: "simt", 5: "flash_attn"}
 ATTN_FLAG_COMPOSED = 0x1
+ATTN_FLAG_ONE_QTILE, ATTN_FLAG_TWO_QTILE = 0x2, 0x4
 MAX_UNARY = 8
 MAX_PEERS = 8
 IPC_HANDLE_BYTES = 64

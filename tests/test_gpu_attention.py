@@ -122,3 +122,29 @@ def test_fused_kernel_one_launch_and_key_limit():
     assert L.lib().ojx_kernel_launch_count() - n0 == 1
     ref = O.attention(host_bits(q), host_bits(k), host_bits(v), dtype=O.BF16, max_keys=2048)
     assert rel_l2(capped, ref) <= 1e-2
+
+
+@pytest.mark.parametrize("B,H,M,N,D,causal", [(1, 2, 128, 128, 64, False), (2, 3, 200, 333, 128, False),
+                                              (1, 4, 256, 256, 128, True), (1, 2, 77, 300, 64, True),
+                                              (2, 2, 1, 1000, 128, False), (1, 1, 640, 1100, 64, True),
+                                              (1, 2, 384, 384, 128, True)])
+@pytest.mark.parametrize("qtiles", [1, 2])
+def test_fused_kernel_each_query_tiling(B, H, M, N, D, causal, qtiles):
+    """Both fused kernels (128 queries per CTA, and two 128-query tiles per CTA in
+    ping-pong), forced through the C-ABI flags, against the oracle."""
+    dev = torch.device("cuda", 0)
+    g = torch.Generator().manual_seed(5 * M + N + D + qtiles)
+    q, k, v = (torch.randn(B, H, x, D, generator=g).bfloat16() for x in (M, N, N))
+    qd, kd, vd = (t.to(dev) for t in (q, k, v))
+    out = torch.full((B, H, M, D), float("nan"), device=dev, dtype=torch.bfloat16)
+    flags = L.ATTN_FLAG_ONE_QTILE if qtiles == 1 else L.ATTN_FLAG_TWO_QTILE
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    L.check(L.lib().ojx_attention(out.data_ptr(), qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), L.BF16,
+                                  B, H, M, N, D, 1.0 / D ** 0.5, int(causal), 0, flags, stream),
+            "ojx_attention")
+    assert L.ROUTES[L.lib().ojx_last_route()] == "flash_attn"
+    torch.cuda.synchronize()
+    got = out.float().cpu().numpy()
+    assert np.isfinite(got).all()
+    ref = O.attention(host_bits(q), host_bits(k), host_bits(v), causal=causal, dtype=O.BF16, max_keys=0)
+    assert rel_l2(got, ref) <= 1e-2, rel_l2(got, ref)
