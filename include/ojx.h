@@ -302,8 +302,8 @@ int ojx_attention(void* out, const void* q, const void* k, const void* v, int32_
                   int32_t causal, int64_t max_keys, int32_t flags, ojx_stream s);
 #define OJX_ATTN_FLAG_COMPOSED 0x1 /* GEMM + softmax + GEMM even where the fused kernel applies */
 #define OJX_ATTN_FLAG_ONE_QTILE 0x2 /* fused kernel with 128 queries per CTA */
-#define OJX_ATTN_FLAG_TWO_QTILE 0x4 /* fused kernel with two 128-query tiles per CTA (ping-pong);
-                                       without either flag the library picks by wave count */
+#define OJX_ATTN_FLAG_TWO_QTILE 0x4 /* fused kernel with two 128-query tiles per CTA (ping-pong;
+                                       the default) */
 
 /* ── graph capture and replay ──────────────────────────────────────────────
  * Replaces torchcl/jit/graph_runner.py: `capture_graph` (:70-86) records the

@@ -3,19 +3,17 @@
 // queries); the scores never leave the SM.
 //
 //   warp 0       TMA producers (lane 0: both Q tiles once, then K_j; lane 1: V_j;
-//                128 keys per tile) into 2-stage rings (rank-3 maps: d, row, problem).
-//   warp 1       MMA issuer, in this order per key tile j:
-//                  PV_0(j)  O_0 += P_0(j) V_j     (once softmax 0 has written P_0(j))
-//                  S_0(j+1) = Q_0 K_{j+1}^T       (into S_0's buffer; P_0(j) was read)
-//                  PV_1(j), S_1(j+1)              (the same for query tile 1)
-//                so the tensor core runs tile 1's MMAs while softmax 0 works on its
-//                next scores, and tile 0's while softmax 1 works.  One thread issues
-//                every MMA, in order.
+//                128 keys per tile) into rings of 2 K stages and 1 (D=128) or 2 V
+//                stages (rank-3 maps: d, row, problem).
+//   warp 1       MMA issuer.  S_t(j+1) = Q_t K_{j+1}^T is issued into S_t's buffer as
+//                soon as softmax t has copied S_t(j) into registers (s_free), so it
+//                runs under the rest of that softmax; O_t += P_t(j) V_j once softmax
+//                t has written P_t(j) (p_full).  One thread issues every MMA, in order.
 //   warps 2-5    softmax of query tile 0, warps 6-9 of tile 1: one query row per
 //                thread (TMEM lane quarter w%4), the whole 128-key score row in
 //                registers, so no exchange between threads.  Each writes its row of
-//                P_t(j) as packed 16-bit pairs over the first 64 columns of S_t's
-//                buffer, rescales its row of O_t when the running maximum grows by
+//                P_t(j) to shared memory (K-major, 128-byte swizzle: the PV MMA's A
+//                operand), rescales its row of O_t when the running maximum grows by
 //                more than 2^8, and finally stores O_t / (sum + 1e-6) (the
 //                reference's denominator) to HBM.
 //
@@ -33,18 +31,24 @@ namespace ojx {
 constexpr int F2_BM = 128;       // query rows per tile (MMA M)
 constexpr int F2_QT = 2;         // query tiles per CTA
 constexpr int F2_BN = 128;       // keys per tile
-constexpr int F2_ST = 2;         // K/V ring stages
+constexpr int F2_KST = 2;        // K ring stages
 constexpr int F2_THREADS = 320;  // producer, MMA, 2 x 4 softmax warps
 
 template <int D>
 struct F2Layout {
   static constexpr int DB = D / 64;                       // 64-wide d blocks (128-byte rows)
+  static constexpr int VST = D == 128 ? 1 : 2;            // V ring stages (shared memory is full at D=128)
   static constexpr int QT_BYTES = F2_BM * D * 2;          // one query tile: DB sub-tiles of 128 x 128 B
+  static constexpr int P_BYTES = F2_BM * F2_BN * 2;       // one P tile: 2 key blocks of 128 rows x 128 B
   static constexpr int K_BYTES = F2_BN * D * 2;
   static constexpr int V_BYTES = F2_BN * D * 2;           // 2 key blocks x DB d blocks of 64 x 64
-  static constexpr int STAGE_BYTES = K_BYTES + V_BYTES;
   static constexpr int BAR_BYTES = 256;
-  static constexpr int SMEM = F2_QT * QT_BYTES + F2_ST * STAGE_BYTES + BAR_BYTES + 1024;
+  static constexpr int OFF_P = F2_QT * QT_BYTES;
+  static constexpr int OFF_K = OFF_P + F2_QT * P_BYTES;
+  static constexpr int OFF_V = OFF_K + F2_KST * K_BYTES;
+  static constexpr int OFF_BAR = OFF_V + VST * V_BYTES;
+  static constexpr int SMEM = OFF_BAR + BAR_BYTES + 1024;
+  static_assert(SMEM <= 227 * 1024, "shared memory");
   static constexpr uint32_t TMEM_COLS = 512;
   static_assert(2 * F2_BN + 2 * D <= 512, "tensor memory layout");
 };
@@ -73,21 +77,26 @@ __global__ void __launch_bounds__(F2_THREADS, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const uint32_t sbase = smem_u32(smem);
   const uint32_t sQ = sbase;
-  const uint32_t sKV = sQ + F2_QT * L::QT_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + F2_QT * L::QT_BYTES + F2_ST * L::STAGE_BYTES);
+  const uint32_t sP = sbase + L::OFF_P;
+  const uint32_t sK0 = sbase + L::OFF_K;
+  const uint32_t sV0 = sbase + L::OFF_V;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
   const uint32_t bar0 = smem_u32(bars);
+  constexpr int VST = L::VST;
   const uint32_t q_full = bar0;
   auto k_full = [&](int s) { return bar0 + 8u * (1 + s); };
-  auto k_empty = [&](int s) { return bar0 + 8u * (1 + F2_ST + s); };
-  auto v_full = [&](int s) { return bar0 + 8u * (1 + 2 * F2_ST + s); };
-  auto v_empty = [&](int s) { return bar0 + 8u * (1 + 3 * F2_ST + s); };
-  auto s_full = [&](int t) { return bar0 + 8u * (1 + 4 * F2_ST + t); };
-  auto p_full = [&](int t) { return bar0 + 8u * (3 + 4 * F2_ST + t); };
-  auto pv_done = [&](int t) { return bar0 + 8u * (5 + 4 * F2_ST + t); };
-  const uint32_t done_bar = bar0 + 8u * (7 + 4 * F2_ST);
-  volatile int* s_abort = reinterpret_cast<volatile int*>(bars + 8 + 4 * F2_ST);
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 9 + 4 * F2_ST);
-  static_assert((10 + 4 * F2_ST) * 8 <= L::BAR_BYTES, "barrier area");
+  auto k_empty = [&](int s) { return bar0 + 8u * (1 + F2_KST + s); };
+  auto v_full = [&](int s) { return bar0 + 8u * (1 + 2 * F2_KST + s); };
+  auto v_empty = [&](int s) { return bar0 + 8u * (1 + 2 * F2_KST + VST + s); };
+  constexpr int B1 = 1 + 2 * F2_KST + 2 * VST;  // per-tile barriers from here
+  auto s_full = [&](int t) { return bar0 + 8u * (B1 + t); };
+  auto s_free = [&](int t) { return bar0 + 8u * (B1 + 2 + t); };
+  auto p_full = [&](int t) { return bar0 + 8u * (B1 + 4 + t); };
+  auto pv_done = [&](int t) { return bar0 + 8u * (B1 + 6 + t); };
+  const uint32_t done_bar = bar0 + 8u * (B1 + 8);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(bars + B1 + 9);
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + B1 + 10);
+  static_assert((B1 + 11) * 8 <= L::BAR_BYTES, "barrier area");
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // heaviest (last, for causal) query blocks first
@@ -99,14 +108,17 @@ __global__ void __launch_bounds__(F2_THREADS, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < F2_ST; ++s) {
+    for (int s = 0; s < F2_KST; ++s) {
       mbar_init(k_full(s), 1);
       mbar_init(k_empty(s), 1);
+    }
+    for (int s = 0; s < VST; ++s) {
       mbar_init(v_full(s), 1);
       mbar_init(v_empty(s), 1);
     }
     for (int t = 0; t < F2_QT; ++t) {
       mbar_init(s_full(t), 1);
+      mbar_init(s_free(t), 4);
       mbar_init(p_full(t), 4);
       mbar_init(pv_done(t), 1);
     }
@@ -141,17 +153,19 @@ __global__ void __launch_bounds__(F2_THREADS, 1)
           for (int db = 0; db < L::DB; ++db)
             tma_load_3d(sQ + t * L::QT_BYTES + db * 16384, &tmQ, q_full, db * 64, q0 + t * F2_BM, bh);
       }
+      const int nst = is_k ? F2_KST : VST;
       for (int j = 0; j < kv_tiles; ++j) {
-        const int st = j % F2_ST;
-        const uint32_t ph = static_cast<uint32_t>(j / F2_ST) & 1u;
-        const uint32_t sK = sKV + st * L::STAGE_BYTES, sV = sK + L::K_BYTES;
+        const int st = j % nst;
+        const uint32_t ph = static_cast<uint32_t>(j / nst) & 1u;
         if (is_k) {
+          const uint32_t sK = sK0 + st * L::K_BYTES;
           if (!mbar_wait(k_empty(st), ph ^ 1u, p.budget, s_abort)) break;
           mbar_arrive_expect_tx(k_full(st), L::K_BYTES);
 #pragma unroll
           for (int db = 0; db < L::DB; ++db)
             tma_load_3d(sK + db * 16384, &tmK, k_full(st), db * 64, j * F2_BN, bh);
         } else {
+          const uint32_t sV = sV0 + st * L::V_BYTES;
           if (!mbar_wait(v_empty(st), ph ^ 1u, p.budget, s_abort)) break;
           mbar_arrive_expect_tx(v_full(st), L::V_BYTES);
 #pragma unroll
@@ -166,7 +180,7 @@ __global__ void __launch_bounds__(F2_THREADS, 1)
       }
       // Let every copy this thread issued land before the CTA may exit.
       if (is_k) mbar_wait_drain(q_full, 0, p.budget);
-      for (int s = 0; s < F2_ST; ++s)
+      for (int s = 0; s < nst; ++s)
         if ((issued >> s) & 1u)
           mbar_wait_drain(is_k ? k_full(s) : v_full(s), (issued_parity >> s) & 1u, p.budget);
     }
@@ -179,7 +193,7 @@ __global__ void __launch_bounds__(F2_THREADS, 1)
       bool ok = mbar_wait(q_full, 0, p.budget, s_abort);
       // S_t(j) = Q_t K_j^T into S_t's buffer (K_j's stage must be full)
       auto issue_s = [&](int t, int j) {
-        const uint32_t sK = sKV + (j % F2_ST) * L::STAGE_BYTES;
+        const uint32_t sK = sK0 + (j % F2_KST) * L::K_BYTES;
         const uint32_t sQt = sQ + t * L::QT_BYTES;
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks) {
@@ -189,15 +203,16 @@ __global__ void __launch_bounds__(F2_THREADS, 1)
         }
         mma_commit(s_full(t));
       };
-      // O_t += P_t(j) V_j (P_t in the first 64 columns of S_t's buffer)
+      // O_t += P_t(j) V_j (P_t K-major in shared memory)
       auto issue_pv = [&](int t, int j) {
-        const uint32_t sV = sKV + (j % F2_ST) * L::STAGE_BYTES + L::K_BYTES;
+        const uint32_t sV = sV0 + (j % VST) * L::V_BYTES;
+        const uint32_t sPt = sP + t * L::P_BYTES;
 #pragma unroll
         for (int ks = 0; ks < F2_BN / 16; ++ks) {
+          const uint64_t a = make_sw128_desc(sPt + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024);
           const uint64_t b =
               make_sw128_desc(sV + (ks >> 2) * (L::DB * 8192) + (ks & 3) * 2048, 8192, 1024);
-          mma_f16_ts(tmem + 2 * F2_BN + t * D, tmem + t * F2_BN + ks * 8, b, IDESC_PV,
-                     (j > 0 || ks > 0) ? 1u : 0u);
+          mma_f16(tmem + 2 * F2_BN + t * D, a, b, IDESC_PV, (j > 0 || ks > 0) ? 1u : 0u);
         }
         mma_commit(pv_done(t));
       };
@@ -209,22 +224,27 @@ __global__ void __launch_bounds__(F2_THREADS, 1)
         mma_commit(k_empty(0));
       }
       for (int j = 0; j < kv_tiles && ok; ++j) {
-        const int st = j % F2_ST;
         const bool more = j + 1 < kv_tiles;
-        if (!(ok = mbar_wait(v_full(st), static_cast<uint32_t>(j / F2_ST) & 1u, p.budget, s_abort))) break;
-        if (more && !(ok = mbar_wait(k_full((j + 1) % F2_ST), static_cast<uint32_t>((j + 1) / F2_ST) & 1u,
+        if (more && !(ok = mbar_wait(k_full((j + 1) % F2_KST), static_cast<uint32_t>((j + 1) / F2_KST) & 1u,
                                      p.budget, s_abort)))
           break;
 #pragma unroll
         for (int t = 0; t < F2_QT; ++t) {
+          if (more) {  // S_t(j) is in registers: compute S_t(j+1) under the rest of softmax t
+            if (!(ok = mbar_wait(s_free(t), static_cast<uint32_t>(j) & 1u, p.budget, s_abort))) break;
+            tc_fence_after();
+            issue_s(t, j + 1);
+          }
+          // V_j (with one V stage, loaded once PV_1(j-1) finished) only gates the PVs
+          if (t == 0 && !(ok = mbar_wait(v_full(j % VST), static_cast<uint32_t>(j / VST) & 1u, p.budget, s_abort)))
+            break;
           if (!(ok = mbar_wait(p_full(t), static_cast<uint32_t>(j) & 1u, p.budget, s_abort))) break;
           tc_fence_after();
           issue_pv(t, j);
-          if (more) issue_s(t, j + 1);  // after PV_t(j), which reads P_t(j) from the same buffer
         }
         if (!ok) break;
-        mma_commit(v_empty(st));
-        if (more) mma_commit(k_empty((j + 1) % F2_ST));
+        if (more) mma_commit(k_empty((j + 1) % F2_KST));
+        mma_commit(v_empty(j % VST));
       }
       // Every MMA issued above must complete before TMEM is released.
       mma_commit(done_bar);
@@ -257,6 +277,10 @@ __global__ void __launch_bounds__(F2_THREADS, 1)
       for (int c = 0; c < F2_BN; c += 16)
         tmem_ld16(trow + s_col + c, *reinterpret_cast<uint32_t(*)[16]>(&r[c]));
       tmem_wait_ld();
+      // S_t(j) is in registers: the MMA warp may compute S_t(j+1) into the buffer.
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(s_free(t));
       // Row maximum (log2 domain), 8 independent accumulators.  The running
       // maximum is only raised when the tile's exceeds it by more than 8 (a
       // factor 256): terms stay below 2^8, and O is rescaled only on those steps.
@@ -279,40 +303,8 @@ __global__ void __launch_bounds__(F2_THREADS, 1)
       const float m_new = raise ? mx : m_run;
       const float m_use = m_new == -INFINITY ? 0.0f : m_new;
       const float alpha = raise ? f2_exp2(m_run - m_use) : 1.0f;  // 0 on the first tile
-      // P = 2^(s * scale - m) as 16-bit pairs, 32 keys (16 packed columns) at a
-      // time over the first 64 columns of S_t's buffer; all scores are already in
-      // registers.
-      float sum8[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) sum8[i] = 0.0f;
-#pragma unroll
-      for (int c = 0; c < F2_BN; c += 32) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          float e0 = f2_exp2(fmaf(__uint_as_float(r[c + i]), p.scale_log2, -m_use));
-          float e1 = f2_exp2(fmaf(__uint_as_float(r[c + i + 1]), p.scale_log2, -m_use));
-          if (!full) {
-            e0 = c + i < n_vis ? e0 : 0.0f;
-            e1 = c + i + 1 < n_vis ? e1 : 0.0f;
-          }
-          sum8[(i >> 1) & 7] += e0 + e1;
-          if (FMT == 1) {
-            const __nv_bfloat162 h = __floats2bfloat162_rn(e0, e1);
-            pk[i / 2] = *reinterpret_cast<const uint32_t*>(&h);
-          } else {
-            const __half2 h = __floats2half2_rn(e0, e1);
-            pk[i / 2] = *reinterpret_cast<const uint32_t*>(&h);
-          }
-        }
-        tmem_st16(trow + s_col + c / 2, pk);
-      }
-      const float sum = ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) +
-                        ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
-      l_run = l_run * alpha + sum;
-      m_run = m_new;
-      // PV_t(j-1) must be done before O_t is rescaled (PV_t(j) waits for this
-      // tile's arrival below); usually it finished long before.
+      // PV_t(j-1) must be done: it reads P_t's buffer, and O_t is rescaled below
+      // (PV_t(j) waits for this tile's arrival); usually it finished long before.
       bool o_ready = true;
       if (j > 0) {
         o_ready = mbar_wait(pv_done(t), static_cast<uint32_t>(j - 1) & 1u, p.budget, s_abort);
@@ -322,6 +314,42 @@ __global__ void __launch_bounds__(F2_THREADS, 1)
         ok = false;
         break;
       }
+      // P = 2^(s * scale - m) as 16-bit pairs into P_t's row: keys 8c .. 8c+7 are
+      // 16-byte chunk c%8 of key block c/8 (128-byte swizzle, the MMA's K-major A)
+      float sum8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) sum8[i] = 0.0f;
+      const uint32_t prow = sP + t * L::P_BYTES + row * 128;
+#pragma unroll
+      for (int c = 0; c < F2_BN / 8; ++c) {
+        uint32_t pk[4];
+#pragma unroll
+        for (int i = 0; i < 8; i += 2) {
+          const int kk = 8 * c + i;
+          float e0 = f2_exp2(fmaf(__uint_as_float(r[kk]), p.scale_log2, -m_use));
+          float e1 = f2_exp2(fmaf(__uint_as_float(r[kk + 1]), p.scale_log2, -m_use));
+          if (!full) {
+            e0 = kk < n_vis ? e0 : 0.0f;
+            e1 = kk + 1 < n_vis ? e1 : 0.0f;
+          }
+          sum8[(kk >> 1) & 7] += e0 + e1;
+          if (FMT == 1) {
+            const __nv_bfloat162 h = __floats2bfloat162_rn(e0, e1);
+            pk[i / 2] = *reinterpret_cast<const uint32_t*>(&h);
+          } else {
+            const __half2 h = __floats2half2_rn(e0, e1);
+            pk[i / 2] = *reinterpret_cast<const uint32_t*>(&h);
+          }
+        }
+        const uint32_t a = prow + (c >> 3) * 16384 + (((c & 7) ^ (row & 7)) << 4);
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(pk[0]), "r"(pk[1]),
+                     "r"(pk[2]), "r"(pk[3])
+                     : "memory");
+      }
+      const float sum = ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) +
+                        ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
+      l_run = l_run * alpha + sum;
+      m_run = m_new;
       if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
 #pragma unroll 1
         for (int c = 0; c < D; c += 16) {
@@ -333,7 +361,8 @@ __global__ void __launch_bounds__(F2_THREADS, 1)
           tmem_st16(trow + o_col + c, o);
         }
       }
-      tmem_wait_st();  // P_t(j) (and a rescaled O_t) written before PV_t(j) may read them
+      tmem_wait_st();            // a rescaled O_t written before PV_t(j) adds to it
+      fence_proxy_async_smem();  // P_t(j) (generic-proxy stores) -> visible to the MMA
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full(t));
