@@ -649,9 +649,10 @@ def run_attention(args):
     import torch
     from torchcl import _lib as L
 
-    parts = [int(x) for x in args.attn.split(",")]
-    B, H, M, N, D = parts[:5]
-    causal = len(parts) > 5 and parts[5] != 0
+    parts = args.attn.split(",")
+    B, H, M, N, D = (int(x) for x in parts[:5])
+    # the sixth field is the word "causal" or a 0/1 flag
+    causal = len(parts) > 5 and parts[5].strip().lower() not in ("0", "", "false")
     lib = L.lib()
     torch.cuda.set_device(0)
     L.check(lib.ojx_init(0, ctypes.byref(L.DeviceInfo())), "ojx_init")
