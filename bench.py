@@ -781,7 +781,10 @@ def main() -> int:
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--gather", default="p2p", choices=["p2p", "nccl"],
                     help="multi-GPU: all-gather fused into the GEMM epilogue (p2p) or NCCL")
-    ap.add_argument("--m", type=int, default=None, help="override M (e.g. cfg4 M in {1,4,16})")
+    # --decode-rows is the spelling to use under torchrun, whose parser takes a bare
+    # --m for an abbreviation of its own options
+    ap.add_argument("--m", "--decode-rows", dest="m", type=int, default=None,
+                    help="override M (e.g. cfg4 M in {1,4,16})")
     ap.add_argument("--size", type=int, default=None, help="override M=N=K (cfg2 sweep)")
     ap.add_argument("--attn", default=None,
                     help="one GPU: time fused attention, 'B,H,M,N,D[,causal]' (bf16)")
