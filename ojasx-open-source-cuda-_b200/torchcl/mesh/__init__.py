@@ -42,6 +42,30 @@ def column_range(N: int, world: int, rank: int) -> tuple[int, int]:
     return rank * w, (rank + 1) * w
 
 
+# Smallest GEMM (2*M*N*K flop) worth sharding.  A sharded step pays a fixed gather and
+# completion-barrier cost (~53 us per step on 8 B200s: the 8-way cfg4 M=1 step took
+# 81.7 us around a 28.7 us kernel).  At ~1.2 PFLOP/s per GPU, sharding over 8 ranks
+# saves 7/8 of the one-GPU time, which covers that cost from ~7e10 flop; 1e11 leaves
+# margin.  OJX_SHARD_MIN_FLOPS overrides it.
+SHARD_MIN_FLOPS = 1e11
+
+
+def should_shard(M: int, N: int, K: int, world: int, min_flops: float | None = None) -> bool:
+    """Static route choice for a GEMM on a group of `world` GPUs (replaces the
+    reference's per-call profiling dispatch, torchcl/liquid/dispatch.py:46-146).
+
+    Shard the columns only when there is more than one rank, N splits evenly, the
+    GEMM is not a decode shape (M <= 16 streams W from HBM and is launch-latency
+    bound per rank once split), and its flop count reaches the threshold.
+    Otherwise the GEMM runs whole on one GPU."""
+    import os
+    if world <= 1 or M <= 16 or N % world:
+        return False
+    if min_flops is None:
+        min_flops = float(os.environ.get("OJX_SHARD_MIN_FLOPS", SHARD_MIN_FLOPS))
+    return 2.0 * M * N * K >= min_flops
+
+
 def assemble_row_major(gathered: torch.Tensor, world: int, M: int, n_local: int,
                        out: torch.Tensor | None = None) -> torch.Tensor:
     """[P][M][N/P] (the all_gather_into_tensor layout) -> row-major [M, P*N/P]."""

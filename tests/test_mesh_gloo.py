@@ -111,3 +111,23 @@ def test_column_range_rules():
         column_range(100, 8, 0)
     with pytest.raises(ValueError):
         column_range(64, 2, 2)
+
+
+def test_should_shard_routes(monkeypatch):
+    """Config 5 (32768^3) shards; config 4 decode shapes and config 3 on one rank
+    stay whole; an uneven column split never shards; the env threshold applies."""
+    import sys
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                                    "ojasx-open-source-cuda-_b200"))
+    from torchcl.mesh import should_shard
+    monkeypatch.delenv("OJX_SHARD_MIN_FLOPS", raising=False)
+    assert should_shard(32768, 32768, 32768, 8)
+    assert should_shard(8192, 11008, 4096, 2)
+    assert not should_shard(8192, 11008, 4096, 1)
+    for m in (1, 4, 16):
+        assert not should_shard(m, 14336, 4096, 8)
+    assert not should_shard(512, 512, 512, 8)
+    assert not should_shard(4096, 1000, 4096, 8)
+    monkeypatch.setenv("OJX_SHARD_MIN_FLOPS", "1e8")
+    assert should_shard(512, 512, 512, 8)
+    assert not should_shard(512, 512, 512, 8, min_flops=1e12)
