@@ -641,6 +641,17 @@ def run_batched(args, cfg):
     return 0
 
 
+def parse_attn_spec(spec: str) -> tuple[int, int, int, int, int, bool]:
+    """'B,H,M,N,D[,causal]' -> (B, H, M, N, D, causal).  The sixth field is the
+    word "causal" or a 0/1 flag."""
+    parts = [x.strip() for x in spec.split(",")]
+    if len(parts) not in (5, 6):
+        raise ValueError(f"--attn wants B,H,M,N,D[,causal], got {spec!r}")
+    B, H, M, N, D = (int(x) for x in parts[:5])
+    causal = len(parts) == 6 and parts[5].lower() not in ("0", "", "false")
+    return B, H, M, N, D, causal
+
+
 def run_attention(args):
     """`--attn B,H,M,N,D[,causal]` on one GPU: torchcl.fused_attention's kernel
     through the C-ABI (ojx_attention) on device-resident bf16 Q, K, V; the fused
@@ -649,10 +660,7 @@ def run_attention(args):
     import torch
     from torchcl import _lib as L
 
-    parts = args.attn.split(",")
-    B, H, M, N, D = (int(x) for x in parts[:5])
-    # the sixth field is the word "causal" or a 0/1 flag
-    causal = len(parts) > 5 and parts[5].strip().lower() not in ("0", "", "false")
+    B, H, M, N, D, causal = parse_attn_spec(args.attn)
     lib = L.lib()
     torch.cuda.set_device(0)
     L.check(lib.ojx_init(0, ctypes.byref(L.DeviceInfo())), "ojx_init")
