@@ -126,8 +126,11 @@ def _dist_setup():
 
 # ── CPU baseline (reference arm and the cpu_baseline field) ───────────────────
 
-def cpu_baseline(cfg: dict, steps: int = 1) -> dict:
-    """Time the oracle port on a bounded sample of the workload, all host threads."""
+def cpu_baseline(cfg: dict, steps: int = 1, min_seconds: float = 0.0) -> dict:
+    """Time the oracle port on a bounded sample of the workload, all host threads.
+
+    Runs `steps` samples, and more (at most 50) until `min_seconds` of CPU work
+    have been timed; reports the median sample."""
     import numpy as np
     from oracle import build_oracle
     build_oracle.build_oracle()
@@ -135,8 +138,8 @@ def cpu_baseline(cfg: dict, steps: int = 1) -> dict:
     rng = np.random.default_rng(cfg["seed"])
     K = cfg["K"]
     # sample: an [ms, ns] block of C with the full K (ascending-k fp32 accumulation)
-    ms = min(cfg["M"], 256 if K >= 16384 else 512)
-    ns = min(cfg["N"], 256 if K >= 16384 else 1024)
+    ms = min(cfg["M"], 1024)
+    ns = min(cfg["N"], 1024)
     A = rng.standard_normal((ms, K), dtype=np.float32)
     B = (rng.standard_normal((K, ns), dtype=np.float32) * cfg["w_scale"]).astype(np.float32)
     bias = rng.standard_normal(ns, dtype=np.float32) * cfg["b_scale"]
@@ -146,7 +149,7 @@ def cpu_baseline(cfg: dict, steps: int = 1) -> dict:
     dt = O.BF16 if half else O.F32
     threads = os.cpu_count() or 1
     times = []
-    for _ in range(max(1, steps)):
+    while len(times) < max(1, steps) or (sum(times) < min_seconds and len(times) < 50):
         t0 = time.perf_counter()
         O.gemm(A, B, dtype_a=dt, dtype_b=dt, dtype_c=dt, operand=bias, operand_kind="row",
                operand_dtype=dt, unary=[cfg["act"]], threads=threads)
@@ -375,7 +378,7 @@ def run_ours(args, cfg, world, rank, local):
     graph = graph_measure(args, cfg, A, Ws[0], biases[0], dev) if args.graph and world == 1 else None
 
     if rank == 0:
-        cb = cpu_baseline(cfg, 1) if world == 1 else None
+        cb = cpu_baseline(cfg, 1, min_seconds=10.0) if world == 1 else None
         line = {"metric": _metric(cfg), "value": value, "unit": "TFLOP/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
