@@ -1,6 +1,6 @@
 """Generate the golden fixtures in tests/golden/ from the OjasX reference itself.
 
-    python tests/golden/make_golden.py [--ref-root /root/reference]
+    python tests/golden/make_golden.py [--ref-root <OjasX checkout>]
 
 Run in the development container (the reference tree is not present on GPU boxes;
 the fixtures it writes are committed).  Two sources of truth are used:
