@@ -126,40 +126,74 @@ def _dist_setup():
 
 # ── CPU baseline (reference arm and the cpu_baseline field) ───────────────────
 
-def cpu_baseline(cfg: dict, steps: int = 1, min_seconds: float = 0.0) -> dict:
+def cpu_baseline(cfg: dict, steps: int = 1, min_seconds: float = 0.0, same_inputs=None) -> dict:
     """Time the oracle port on a bounded sample of the workload, all host threads.
 
     Runs `steps` samples, and more (at most 50) until `min_seconds` of CPU work
-    have been timed; reports the median sample."""
+    have been timed; reports the median sample.  The sample is the block
+    C[0:ms, 0:ns] (ms, ns <= 1024) with the full K.
+
+    same_inputs (our arm, one GPU): (A, W, bias, C) device tensors of the timed
+    run.  The port then runs on copies of A[0:ms, :], W[:, 0:ns] and bias[0:ns],
+    and its output block is also the parity check of the GPU's C[0:ms, 0:ns]
+    (returned under "parity"); without it (the reference arm) the sample's inputs
+    are drawn on the host."""
     import numpy as np
     from oracle import build_oracle
     build_oracle.build_oracle()
     from oracle import oracle as O
-    rng = np.random.default_rng(cfg["seed"])
     K = cfg["K"]
-    # sample: an [ms, ns] block of C with the full K (ascending-k fp32 accumulation)
     ms = min(cfg["M"], 1024)
     ns = min(cfg["N"], 1024)
-    A = rng.standard_normal((ms, K), dtype=np.float32)
-    B = (rng.standard_normal((K, ns), dtype=np.float32) * cfg["w_scale"]).astype(np.float32)
-    bias = rng.standard_normal(ns, dtype=np.float32) * cfg["b_scale"]
     half = cfg["dtype"] == "bf16"
-    if half:
-        A, B, bias = O.bf16_bits(A), O.bf16_bits(B), O.bf16_bits(bias)
     dt = O.BF16 if half else O.F32
+    if same_inputs is not None:
+        import torch
+        Ad, Wd, bd, Cd = same_inputs
+
+        def host(t):
+            t = t.contiguous().cpu()
+            return t.view(torch.int16).numpy().view(np.uint16) if half else t.numpy()
+        A, B, bias = host(Ad[:ms]), host(Wd[:, :ns]), host(bd[:ns])
+        gpu = Cd[:ms, :ns].float().cpu().numpy().astype(np.float64)
+    else:
+        rng = np.random.default_rng(cfg["seed"])
+        A = rng.standard_normal((ms, K), dtype=np.float32)
+        B = (rng.standard_normal((K, ns), dtype=np.float32) * cfg["w_scale"]).astype(np.float32)
+        bias = rng.standard_normal(ns, dtype=np.float32) * cfg["b_scale"]
+        if half:
+            A, B, bias = O.bf16_bits(A), O.bf16_bits(B), O.bf16_bits(bias)
+        gpu = None
     threads = os.cpu_count() or 1
     times = []
+    out = None
     while len(times) < max(1, steps) or (sum(times) < min_seconds and len(times) < 50):
         t0 = time.perf_counter()
-        O.gemm(A, B, dtype_a=dt, dtype_b=dt, dtype_c=dt, operand=bias, operand_kind="row",
-               operand_dtype=dt, unary=[cfg["act"]], threads=threads)
+        out = O.gemm(A, B, dtype_a=dt, dtype_b=dt, dtype_c=dt, operand=bias, operand_kind="row",
+                     operand_dtype=dt, unary=[cfg["act"]], threads=threads)
         times.append(time.perf_counter() - t0)
     t = statistics.median(times)
     flops = 2.0 * ms * ns * K
-    return {"value": flops / t / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
-            "sample": f"C[0:{ms}, 0:{ns}] with full K={K} ({'bf16 widened to fp32' if half else 'fp32'}, "
-                      f"k ascending, fp32 accumulate, {cfg['act']} epilogue), median of {len(times)}",
-            "seconds_per_sample": t}
+    res = {"value": flops / t / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+           "sample": f"C[0:{ms}, 0:{ns}] with full K={K} ({'bf16 widened to fp32' if half else 'fp32'}, "
+                     f"k ascending, fp32 accumulate, {cfg['act']} epilogue), median of {len(times)}",
+           "seconds_per_sample": t}
+    if gpu is not None:
+        ref = (O.bf16_to_f32(out) if half else out).astype(np.float64)
+        rel = float(np.linalg.norm(gpu - ref) / max(np.linalg.norm(ref), 1e-30))
+        mx = float(np.abs(gpu - ref).max())
+        if half:
+            ok, bar = rel <= 1e-2, "rel-L2 <= 1e-2"
+        else:
+            # max-abs scale ||A||_F ||B||_F / sqrt(MN) of the whole product, on the device
+            Ad, Wd = same_inputs[0], same_inputs[1]
+            scale = float(Ad.double().norm() * Wd.double().norm()) / (cfg["M"] * cfg["N"]) ** 0.5
+            ok = rel <= 1e-5 and mx <= 1e-4 * scale
+            bar = f"rel-L2 <= 1e-5 and max-abs <= 1e-4 * {scale:.4g}"
+        res["parity"] = {"rel_l2": rel, "max_abs": mx, "bar": bar, "pass": bool(ok),
+                         "sample": f"C[0:{ms}, 0:{ns}] of the timed run's output (full K) against "
+                                   f"the oracle on the same device inputs"}
+    return res
 
 
 def run_reference(args, cfg, world, rank):
@@ -222,6 +256,36 @@ def _config_block(args, cfg, world) -> dict:
 
 # ── our implementation ──────────────────────────────────────────────────────
 
+def make_inputs(cfg: dict, dev, world: int = 1, rank: int = 0):
+    """Seeded synthetic inputs of a config on device `dev`: (A [M,K], this rank's
+    column block of W [K, N/world], its bias slice [N/world]).
+
+    A ~ U(-1,1) or N(0,1); W ~ N(0, w_scale^2); bias ~ N(0, b_scale^2), drawn in
+    that order from one torch.Generator on the device.  W is drawn as `world`
+    column blocks one after another and every rank draws all of them, so the ranks
+    of one run hold slices of one and the same full W and bias.  The GPU parity
+    tests regenerate the one-GPU inputs (world = 1) with this function."""
+    import torch
+    tdt = torch.bfloat16 if cfg["dtype"] == "bf16" else torch.float32
+    M, N, K = cfg["M"], cfg["N"], cfg["K"]
+    Nl = N // world
+    g = torch.Generator(device=dev).manual_seed(cfg["seed"])
+    if cfg["a"] == "uniform":
+        A = (torch.rand(M, K, device=dev, generator=g) * 2 - 1).to(tdt)
+    else:
+        A = torch.randn(M, K, device=dev, generator=g).to(tdt)
+    W = None
+    for r in range(world):
+        blk = (torch.randn(K, Nl, device=dev, generator=g) * cfg["w_scale"]).to(tdt)
+        if r == rank:
+            W = blk
+        else:
+            del blk
+    bias_full = (torch.randn(N, device=dev, generator=g) * cfg["b_scale"]).to(tdt)
+    bias = bias_full[rank * Nl:(rank + 1) * Nl].contiguous()
+    return A, W, bias
+
+
 def run_ours(args, cfg, world, rank, local):
     import torch
     import torch.distributed as dist
@@ -239,21 +303,7 @@ def run_ours(args, cfg, world, rank, local):
     if N % world:
         raise SystemExit(f"N={N} is not divisible by {world} ranks")
     Nl = N // world
-    g = torch.Generator(device=dev).manual_seed(cfg["seed"])
-    if cfg["a"] == "uniform":
-        A = (torch.rand(M, K, device=dev, generator=g) * 2 - 1).to(tdt)
-    else:
-        A = torch.randn(M, K, device=dev, generator=g).to(tdt)
-    # W generated column block by column block so every rank draws the same full W
-    W = None
-    for r in range(world):
-        blk = (torch.randn(K, Nl, device=dev, generator=g) * cfg["w_scale"]).to(tdt)
-        if r == rank:
-            W = blk
-        else:
-            del blk
-    bias_full = (torch.randn(N, device=dev, generator=g) * cfg["b_scale"]).to(tdt)
-    bias = bias_full[rank * Nl:(rank + 1) * Nl].contiguous()
+    A, W, bias = make_inputs(cfg, dev, world, rank)
     n_copies = _w_copies(cfg, world)
     Ws = [W] + [W.clone() for _ in range(n_copies - 1)]
     biases = [bias] + [bias.clone() for _ in range(n_copies - 1)]
@@ -378,7 +428,8 @@ def run_ours(args, cfg, world, rank, local):
     graph = graph_measure(args, cfg, A, Ws[0], biases[0], dev) if args.graph and world == 1 else None
 
     if rank == 0:
-        cb = cpu_baseline(cfg, 1, min_seconds=10.0) if world == 1 else None
+        cb = (cpu_baseline(cfg, 1, min_seconds=10.0, same_inputs=(A, Ws[0], biases[0], C))
+              if world == 1 else None)
         line = {"metric": _metric(cfg), "value": value, "unit": "TFLOP/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
@@ -386,6 +437,7 @@ def run_ours(args, cfg, world, rank, local):
                 "config": _config_block(args, cfg, world), "route": route, "roofline": roof,
                 "cpu_baseline": ({k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
                                  if cb else None),
+                "parity": cb.get("parity") if cb else None,
                 "e2e": e2e, "gpu_launches": int(launches),
                 "clocks": {k: clocks[k] for k in ("sm_mhz", "sm_max_mhz", "reasons")},
                 "clock_samples": clocks.get("samples"), "power_w_max": clocks.get("power_w_max")}
@@ -431,7 +483,7 @@ def e2e_measure(args, lib, L, A, C, M, K, N, es, gemm, gather, world, dev, strea
             gather()
             L.check(lib.ojx_memcpy_d2h(hc.value, C.data_ptr(), c_bytes, sp), "d2h")
 
-    steps = max(2, min(args.steps, 5))
+    steps = max(2, args.steps)
     step()
     torch.cuda.synchronize(dev)
     if world > 1:

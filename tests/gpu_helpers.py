@@ -108,3 +108,77 @@ def assert_half_parity(C, ref, tol=1e-2):
     r = rel_l2(C, ref)
     assert r <= tol, f"rel-L2 {r:.3e} > {tol}"
     return r
+
+
+# ── device-resident operands (the BASELINE-size parity tests) ──────────────────
+
+def device_gemm(A, B, C, *, trans_a=False, trans_b=False, bias=None, unary=(), fp32_mode=0,
+                flags=0) -> str:
+    """C = unary(op(A) @ op(B) + bias[N]) through ojx_gemm on torch CUDA tensors, on
+    torch's current stream; returns the route the library took."""
+    import ctypes
+    from torchcl import _lib as L
+    lib = L.lib()
+    code = {torch.float32: L.F32, torch.bfloat16: L.BF16, torch.float16: L.F16}
+    M = A.shape[1] if trans_a else A.shape[0]
+    K = A.shape[0] if trans_a else A.shape[1]
+    N = B.shape[0] if trans_b else B.shape[1]
+    d = L.GemmDesc()
+    d.M, d.N, d.K = M, N, K
+    d.dtype_a, d.dtype_b, d.dtype_c = code[A.dtype], code[B.dtype], code[C.dtype]
+    d.trans_a, d.trans_b = int(trans_a), int(trans_b)
+    d.a, d.b, d.c = A.data_ptr(), B.data_ptr(), C.data_ptr()
+    if bias is not None:
+        d.operand, d.dtype_operand = bias.data_ptr(), code[bias.dtype]
+        d.operand_kind, d.binary_op = L.OPERAND_ROW, L.BINARY["add"]
+    d.n_unary = len(unary)
+    for i, u in enumerate(unary):
+        d.unary[i] = L.UNARY[u]
+    d.fp32_mode, d.flags = fp32_mode, flags
+    L.check(lib.ojx_gemm(ctypes.byref(d), torch.cuda.current_stream().cuda_stream), "ojx_gemm")
+    route = L.ROUTES.get(lib.ojx_last_route())
+    torch.cuda.synchronize()
+    L.check(lib.ojx_poll_device_error(), "device error")
+    return route
+
+
+def sample_indices(n_total: int, n: int, seed: int) -> np.ndarray:
+    """n distinct indices of [0, n_total), sorted, from a seeded generator (all of
+    them when n >= n_total)."""
+    if n >= n_total:
+        return np.arange(n_total, dtype=np.int64)
+    return np.sort(np.random.default_rng(seed).choice(n_total, size=n, replace=False)).astype(np.int64)
+
+
+def sampled_parity(A, B, C, *, trans_a=False, trans_b=False, bias=None, unary=(), n=64,
+                   seed=0):
+    """(gpu, oracle, rows, cols) for n seeded complete rows and n complete columns of C.
+
+    A, B, C and bias are device tensors.  The oracle computes the sampled rows from
+    op(A)[rows, :] and the whole of op(B), and the sampled columns from the whole of
+    op(A) and op(B)[:, cols] (each element is the same ascending-k dot product as in
+    the full product).  gpu and oracle are the concatenated samples, fp32."""
+    M, N = C.shape
+    rows = sample_indices(M, n, seed)
+    cols = sample_indices(N, n, seed + 1)
+    rt, ct = torch.from_numpy(rows).to(C.device), torch.from_numpy(cols).to(C.device)
+    a_rows = (A[:, rt].t() if trans_a else A[rt]).contiguous().cpu()
+    b_cols = (B[ct].t() if trans_b else B[:, ct]).contiguous().cpu()
+    A_h, B_h = A.cpu(), B.cpu()
+    bias_h = bias.cpu() if bias is not None else None
+    kind = "row" if bias is not None else None
+    ref_r = oracle_gemm(a_rows, B_h, trans_b=trans_b, operand=bias_h, kind=kind, unary=unary,
+                        out_dtype=C.dtype)
+    ref_c = oracle_gemm(A_h, b_cols, trans_a=trans_a,
+                        operand=bias_h[torch.from_numpy(cols)] if bias_h is not None else None,
+                        kind=kind, unary=unary, out_dtype=C.dtype)
+    got_r = C[rt].float().cpu().numpy()
+    got_c = C[:, ct].float().cpu().numpy()
+    gpu = np.concatenate([got_r.ravel(), got_c.ravel()])
+    ref = np.concatenate([ref_r.ravel(), ref_c.ravel()])
+    return gpu, ref, rows, cols
+
+
+def fp32_scale(A, B, M: int, N: int) -> float:
+    """||A||_F ||B||_F / sqrt(M N) of an [M, N] product (the north_star max-abs scale)."""
+    return float(A.double().norm() * B.double().norm()) / float(np.sqrt(M * N))
