@@ -1,4 +1,4 @@
-// gemm_tc.cu — persistent, warp-specialised tcgen05 GEMM with the fused epilogue.
+// gemm_tc.cuh — persistent, warp-specialised tcgen05 GEMM with the fused epilogue.
 //
 // Replaces the reference's matmul_reg_tiled_f32 / matmul_reg_tiled_bias_f32 /
 // linear_forward_tiled_f32 / matmul_tiled_fp16 (torchcl/kernels/matmul.cl:19-224,
@@ -6,7 +6,7 @@
 // (torchcl/jit/compiler.py:99-133): C = epilogue(A·B) in one launch, one store.
 //
 // CTA = 320 threads, one CTA per SM, grid = min(#tiles, #SMs), tiles walked with a
-// stride of gridDim.x in a grouped (8 M-blocks) raster for L2 reuse.
+// stride of gridDim.x in a grouped raster (16 M-blocks per N sweep) for L2 reuse.
 //   warp 0      TMA producer: STAGES-deep ring of 128B-swizzled A/B tiles
 //   warp 1      TMEM owner + single-thread tcgen05.mma issuer
 //   warps 2..9  epilogue: TMEM -> registers -> bias/binary/unary chain -> store;
@@ -66,7 +66,7 @@ struct TcLayout {
   static_assert((2 * STAGES + 6) * 8 + 8 <= BAR_BYTES, "barrier area too small");
 };
 
-// Grouped raster: 8 consecutive M-blocks share each N-block sweep.
+// Grouped raster: GROUP = 16 consecutive M-blocks share each N-block sweep.
 __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int& mb, int& nb) {
   constexpr int GROUP = 16;
   const int span = GROUP * tiles_n;

@@ -31,8 +31,8 @@
 //    calls that run at the same time on the GPU (different streams, no ordering)
 //    race on the array: order them on one stream or synchronise;
 //  * the first call on a device looks up the array's device address
-//    (cudaGetSymbolAddress), clears the counters and sets the kernel's shared-memory
-//    limit; make that first call before capturing a stream.
+//    (cudaGetSymbolAddress) and sets the kernel's shared-memory limit; make that
+//    first call before capturing a stream.
 namespace ojx {
 
 constexpr size_t kNoAllocCounterBytes = 64 * 1024;  // up to 8192 column groups
@@ -53,9 +53,12 @@ static int noalloc_setup(void** out) {
   std::lock_guard<std::mutex> g(g_noalloc_mu);
   if (!g_noalloc_ptr[dev]) {
     void* p = nullptr;
+    // No clearing is needed (or issued: a cudaMemset here would run on the legacy
+    // stream, unordered with a caller's non-blocking stream): a __device__ array
+    // starts zeroed, and the arrival counters are tagged with a launch epoch, so
+    // counts an earlier call left behind never match a new launch's epoch.
     if ((st = cuda_status(cudaGetSymbolAddress(&p, g_noalloc_scratch), "cudaGetSymbolAddress")))
       return st;
-    if ((st = cuda_status(cudaMemset(p, 0, kNoAllocCounterBytes), "clear arrival counters"))) return st;
     const void* kernels[4] = {reinterpret_cast<const void*>(skinny_gemm_kernel<1, 1>),
                               reinterpret_cast<const void*>(skinny_gemm_kernel<1, 0>),
                               reinterpret_cast<const void*>(skinny_gemm_kernel<0, 1>),
@@ -137,7 +140,11 @@ extern "C" int ojx_gemm_skinny_noalloc(const ojx_gemm_desc* in, ojx_stream strea
   if (p.epoch == 0) p.epoch = g_skinny_epoch.fetch_add(1);
   p.budget = g_wait_budget.load();
   p.silence_producer = 0;
-  p.trigger_early = 0;  // plain launch: the next kernel starts after this one completes
+  // This launch must stay a plain one that never lets the next kernel in early:
+  // it does not publish the ranges it writes to the per-stream record the skinny
+  // route consults before loading W ahead of its dependency wait, so a following
+  // eager skinny launch may only overlap a grid that has completed.
+  p.trigger_early = 0;
   p.early_w = 0;
 
   const CUtensorMapDataType tdt =

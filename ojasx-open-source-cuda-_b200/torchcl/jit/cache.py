@@ -1,67 +1,68 @@
-"""Plan cache — the reference's KernelCache (torchcl/jit/cache.py:17-78).
+"""Fusion plans of the elementwise path, built once per op chain.
 
-The reference caches compiled OpenCL kernels per generated source.  libojx has no
-runtime compiler (every kernel is built ahead of time for sm_100a), so what is
-cached is the fusion *plan* — the op-code tuple a fused launch executes — under
-the same keys, with the same LRU, hit/miss statistics and thread safety.
+The reference compiles one OpenCL program per generated kernel source and keeps
+the kernel objects (torchcl/jit/cache.py:17-78); its tests only read the hit
+counter, `get_kernel_cache().stats()["hits"]` (tests/test_jit.py:81-95,
+tests/test_jit_integration.py:28-47).
+
+Nothing is compiled at run time here.  Every chain runs on the one ahead-of-time
+ojx_elementwise kernel, which takes the chain as an array of op codes, so the
+thing worth keeping between calls is that array (building it validates every op
+name and allocates a ctypes array).  A plan depends only on the chain itself
+(binary op and unary op names): not on the element count, the buffers or the
+dtypes.  The cache is therefore keyed by the chain tuple, and it holds at most
+one entry per distinct chain a program fuses, a small and bounded set (the op
+alphabet is fixed and a chain holds at most eight unary ops), so it never evicts.
 """
 from __future__ import annotations
 
-import hashlib
 import threading
-from collections import OrderedDict
-from typing import Any
+from typing import Callable, Hashable
 
 
-class KernelCache:
-    def __init__(self, max_size: int = 512) -> None:
-        self._cache: OrderedDict[str, Any] = OrderedDict()
-        self._max_size = max_size
-        self._lock = threading.Lock()
+class PlanCache:
+    """chain -> plan, built on first use by the caller's `build(chain)`."""
+
+    def __init__(self) -> None:
+        self._plans: dict[Hashable, object] = {}
+        self._build_lock = threading.Lock()
         self._hits = 0
-        self._misses = 0
+        self._builds = 0
 
-    def get(self, key: str):
-        with self._lock:
-            if key in self._cache:
-                self._cache.move_to_end(key)
-                self._hits += 1
-                return self._cache[key]
-            self._misses += 1
-            return None
+    def plan_for(self, chain: Hashable, build: Callable[[Hashable], object]) -> object:
+        plan = self._plans.get(chain)
+        if plan is None:
+            # Builds are serialised so two threads never build the same chain twice;
+            # lookups of chains already present take no lock.
+            with self._build_lock:
+                plan = self._plans.get(chain)
+                if plan is None:
+                    plan = build(chain)  # raises on an unknown op: nothing is stored
+                    self._plans[chain] = plan
+                    self._builds += 1
+                    return plan
+        self._hits += 1
+        return plan
 
-    def put(self, key: str, plan) -> None:
-        with self._lock:
-            if key in self._cache:
-                self._cache.move_to_end(key)
-            elif len(self._cache) >= self._max_size:
-                self._cache.popitem(last=False)
-            self._cache[key] = plan
+    def __contains__(self, chain: Hashable) -> bool:
+        return chain in self._plans
 
-    def clear(self) -> None:
-        with self._lock:
-            self._cache.clear()
-            self._hits = 0
-            self._misses = 0
+    def __len__(self) -> int:
+        return len(self._plans)
 
     def stats(self) -> dict:
-        with self._lock:
-            total = self._hits + self._misses
-            return {"size": len(self._cache), "max_size": self._max_size, "hits": self._hits,
-                    "misses": self._misses,
-                    "hit_rate": f"{self._hits / total:.1%}" if total > 0 else "N/A"}
+        """hits: lookups answered from the cache; misses: plans built; size: chains held."""
+        return {"hits": self._hits, "misses": self._builds, "size": len(self._plans)}
 
-    @staticmethod
-    def make_key(*parts) -> str:
-        raw = ":".join(str(p) for p in parts)
-        return hashlib.sha256(raw.encode()).hexdigest() if len(raw) > 128 else raw
+    def clear(self) -> None:
+        with self._build_lock:
+            self._plans = {}
+            self._hits = self._builds = 0
 
 
-_global_cache: KernelCache | None = None
+_plans = PlanCache()
 
 
-def get_kernel_cache() -> KernelCache:
-    global _global_cache
-    if _global_cache is None:
-        _global_cache = KernelCache()
-    return _global_cache
+def get_kernel_cache() -> PlanCache:
+    """The process-wide plan cache (the reference's accessor name)."""
+    return _plans

@@ -18,7 +18,6 @@ import torch
 
 from torchcl import _lib as L
 from torchcl.jit.cache import get_kernel_cache
-from torchcl.jit.tuner import get_auto_tuner
 from torchcl.ops.engine import ojx_dtype
 from torchcl.runtime.context import get_queue
 
@@ -33,28 +32,29 @@ _UNARY_OPS = {
 _BINARY_OPS = {"add": "a + b", "sub": "a - b", "mul": "a * b", "div": "a / b"}
 
 
+def _build_plan(chain):
+    """(binary op or None, unary names) -> (ctypes op-code array, number of unary ops)."""
+    _, ops = chain
+    for op in ops:
+        if op not in _UNARY_OPS:
+            raise ValueError(f"Unknown unary op for fusion: {op}")
+    if len(ops) > L.MAX_UNARY:
+        raise ValueError(f"at most {L.MAX_UNARY} fused unary ops")
+    codes = [L.UNARY[o] for o in ops]
+    return (ctypes.c_int32 * max(1, len(codes)))(*codes), len(codes)
+
+
 class JITCompiler:
     def __init__(self) -> None:
         self._cache = get_kernel_cache()
-        self._tuner = get_auto_tuner()
 
-    def _plan(self, key: str, ops: Sequence[str]):
-        plan = self._cache.get(key)
-        if plan is None:
-            for op in ops:
-                if op not in _UNARY_OPS:
-                    raise ValueError(f"Unknown unary op for fusion: {op}")
-            if len(ops) > L.MAX_UNARY:
-                raise ValueError(f"at most {L.MAX_UNARY} fused unary ops")
-            codes = [L.UNARY[o] for o in ops]
-            plan = ((ctypes.c_int32 * max(1, len(codes)))(*codes), len(codes))
-            self._cache.put(key, plan)
-        return plan
+    def _plan(self, binary_op, ops: Sequence[str]):
+        return self._cache.plan_for((binary_op, tuple(ops)), _build_plan)
 
     def fuse_elementwise_chain(self, ops: Sequence[str], n: int, input_buffers: list,
                                output_buffer, dtypes=(torch.float32, torch.float32)) -> None:
         """out[i] = ops[-1](...ops[0](in[i])) (compiler.py:64-97)."""
-        codes, n_codes = self._plan(f"fused_unary_{'_'.join(ops)}_{n}", ops)
+        codes, n_codes = self._plan(None, ops)
         din, dout = dtypes
         L.check(L.lib().ojx_elementwise(int(output_buffer), ojx_dtype(dout), int(input_buffers[0]),
                                         ojx_dtype(din), None, 0, 0, codes, n_codes, int(n),
@@ -66,7 +66,7 @@ class JITCompiler:
         """out[i] = unary_ops(a[i] binary_op b[i]) (compiler.py:99-133)."""
         if binary_op not in _BINARY_OPS:
             raise ValueError(f"Unknown binary op for fusion: {binary_op}")
-        codes, n_codes = self._plan(f"fused_{binary_op}_{'_'.join(unary_ops)}_{n}", unary_ops)
+        codes, n_codes = self._plan(binary_op, unary_ops)
         da, db, dout = dtypes
         L.check(L.lib().ojx_elementwise(int(out_buf), ojx_dtype(dout), int(a_buf), ojx_dtype(da),
                                         int(b_buf), ojx_dtype(db), L.BINARY[binary_op], codes,

@@ -1,9 +1,10 @@
 """Launch-parameter heuristics — the reference's AutoTuner (torchcl/jit/tuner.py:18-117).
 
 libojx sizes its own grids (persistent GEMMs use one CTA per SM; elementwise
-kernels use a grid-stride loop over up to 16 CTAs per SM), so these answers are
-informational; they keep the reference's contract (powers of two, tile sizes in
-{4, 8, 16}).
+kernels use a grid-stride loop over up to 16 CTAs per SM), so only the queries
+callers of the reference make are kept (tests/test_jit.py:72-78): the 1-D
+work-group size and the tile size, under the reference's contract (powers of two,
+tile sizes in {4, 8, 16}), plus the device limits.
 """
 from __future__ import annotations
 
@@ -30,12 +31,6 @@ class AutoTuner:
 
     def optimal_tile_size(self, M: int, N: int, K: int) -> int:
         return 16 if min(M, N, K) >= 32 else (8 if min(M, N, K) >= 16 else 4)
-
-    def optimal_matmul_strategy(self, M: int, N: int, K: int) -> str:
-        return "tiled"
-
-    def should_vectorize(self) -> bool:
-        return True
 
     def max_alloc_elements(self, dtype_bytes: int = 4) -> int:
         return (self.info["max_mem_alloc_size_mb"] * 1024 * 1024) // dtype_bytes

@@ -156,6 +156,15 @@ class ShardedGemm:
             d.unary[i] = c
         return d
 
+    def _stream_ctx(self):
+        """torch.distributed collectives run on torch's current stream: make it this
+        object's stream, so that a collective is ordered after the GEMM launched on
+        it (a no-op when no stream was given: the GEMM then runs on the current one)."""
+        import contextlib
+        if self.stream is None or self.stream == torch.cuda.current_stream(self.device).cuda_stream:
+            return contextlib.nullcontext()
+        return torch.cuda.stream(torch.cuda.ExternalStream(self.stream, device=self.device))
+
     def launch(self, a_ptr: int, w_shard_ptr: int, bias_shard_ptr: int | None = None,
                unary=("relu",)) -> None:
         """Enqueue this rank's GEMM (and, for "nccl", the gather) on the stream."""
@@ -170,17 +179,21 @@ class ShardedGemm:
                            self.n_local)
             L.check(self.lib.ojx_gemm(ctypes.byref(d), sp), "ojx_gemm")
             if self.world > 1:
-                dist.all_gather_into_tensor(self.gathered, self.c_local.view(-1), group=self.group)
-                assemble_row_major(self.gathered, self.world, self.M, self.n_local, out=self.c_view())
+                with self._stream_ctx():
+                    dist.all_gather_into_tensor(self.gathered, self.c_local.view(-1), group=self.group)
+                    assemble_row_major(self.gathered, self.world, self.M, self.n_local,
+                                       out=self.c_view())
             else:
                 L.check(self.lib.ojx_memcpy_d2d(self.c_ptr, self.c_local.data_ptr(),
                                                 self.M * self.N * 2, sp), "copy")
 
     def barrier(self) -> None:
-        """Stream-ordered barrier: after it, every rank's writes into C have landed."""
+        """Stream-ordered barrier on this object's stream: work queued on that stream
+        after it sees every rank's writes into C."""
         import torch.distributed as dist
         if self.strategy == "p2p" and self.world > 1:
-            dist.all_reduce(self._flag, group=self.group)
+            with self._stream_ctx():
+                dist.all_reduce(self._flag, group=self.group)
 
     def run(self, a_ptr: int, w_shard_ptr: int, bias_shard_ptr: int | None = None,
             unary=("relu",)) -> None:

@@ -2,6 +2,11 @@
 
     python oracle/build_oracle.py [--ref-root /path/to/OjasX]
 
+The reference tree is taken from --ref-root, else the OJX_REFERENCE_ROOT
+environment variable, else a checkout named `reference` beside this repository;
+when none of them holds the kernels, oracle/_ref is not built (and the tests that
+need it skip).
+
 * oracle/_build/libojx_oracle.so — the C++ restatement (ojx_oracle.cpp), always built.
 * oracle/_ref/libref_kernels_nofma.so and libref_kernels_fma.so — the reference's own
   OpenCL C kernels (torchcl/kernels/{matmul,activation,elementwise,precision}.cl, read
@@ -26,7 +31,7 @@ HERE = pathlib.Path(__file__).resolve().parent
 BUILD = HERE / "_build"
 REF_OUT = HERE / "_ref"
 HARNESS = HERE / "ref_harness"
-DEFAULT_REF_ROOT = os.environ.get("OJX_REFERENCE_ROOT", "/root/reference")
+DEFAULT_REF_ROOT = os.environ.get("OJX_REFERENCE_ROOT") or str(HERE.parent.parent / "reference")
 CXX = os.environ.get("OJX_CXX") or ("/usr/bin/g++" if os.path.exists("/usr/bin/g++") else shutil.which("g++") or "g++")
 BASE = ["-O3", "-march=x86-64-v3", "-fopenmp", "-fPIC", "-shared", "-std=c++17"]
 

@@ -1,9 +1,14 @@
 """ojx_gemm_skinny_noalloc: the decode GEMM for callers that must not have the
 library allocate device memory (engines that reserve the GPU's memory up front,
-loops where an allocation could synchronise the device).  Called through the
-C-ABI and compared with the regular entry point, ojx_gemm (whose skinny route
-takes its scratch from a cudaMalloc-grown workspace), on two calls in a row, so
-the second call runs on the scratch contents the first one left behind.
+loops where an allocation could synchronise the device).
+
+Called through the C-ABI on two different problems in a row, so that the second
+call runs on the scratch contents the first one left behind: its partial-sum slots
+and arrival counters overlap the first call's with different values.  Each call is
+compared with the oracle (the reference's ascending-k fp32 accumulation, then the
+epilogue) and, bit for bit, with the regular entry point ojx_gemm on the same
+inputs: both run the same kernel with the same grid and sum the split-K partials
+in the same fixed order, so only the place the scratch lives differs.
 
 This file is collected last on purpose; it must also pass on its own in a fresh
 process (it initialises the device itself)."""
@@ -13,7 +18,16 @@ import numpy as np
 import pytest
 import torch
 
+from gpu_helpers import oracle_gemm, rel_l2
+
 pytestmark = pytest.mark.gpu
+
+
+def _lib():
+    from torchcl import _lib as L
+    lib = L.lib()
+    L.check(lib.ojx_init(0, ctypes.byref(L.DeviceInfo())), "ojx_init")
+    return lib, L
 
 
 def _upload(lib, L, t: torch.Tensor) -> int:
@@ -33,61 +47,79 @@ def _download(lib, L, ptr: int, shape, dtype) -> torch.Tensor:
     return out
 
 
-@pytest.mark.parametrize("M,N,K,trans_b", [(16, 14336, 4096, False), (1, 1000, 320, True),
-                                           (7, 4096, 2048, False)])
-def test_noalloc_matches_regular_entry_point_twice(M, N, K, trans_b):
-    import sys
-    import pathlib
-    repo = pathlib.Path(__file__).resolve().parents[1]
-    sys.path[:0] = [str(repo), str(repo / "ojasx-open-source-cuda-_b200")]
-    from torchcl import _lib as L
+class _Problem:
+    """One seeded decode problem silu(X @ op(W) + bias), bf16, uploaded to the device."""
 
-    lib = L.lib()
-    L.check(lib.ojx_init(0, ctypes.byref(L.DeviceInfo())), "ojx_init")
-    g = torch.Generator().manual_seed(M * 7 + N + K)
-    X = torch.randn(M, K, generator=g).bfloat16()
-    W = (torch.randn((N, K) if trans_b else (K, N), generator=g) * 0.02).bfloat16()
-    bias = (torch.randn(N, generator=g) * 0.1).bfloat16()
-    px, pw, pb = _upload(lib, L, X), _upload(lib, L, W), _upload(lib, L, bias)
-    out = []
-    for _ in range(3):
-        p = ctypes.c_void_p()
-        L.check(lib.ojx_malloc(M * N * 2, ctypes.byref(p), None), "ojx_malloc")
-        out.append(p.value)
+    def __init__(self, lib, L, M, N, K, trans_b, seed):
+        self.lib, self.L = lib, L
+        self.M, self.N, self.K, self.trans_b = M, N, K, trans_b
+        g = torch.Generator().manual_seed(seed)
+        self.X = torch.randn(M, K, generator=g).bfloat16()
+        self.W = (torch.randn((N, K) if trans_b else (K, N), generator=g) * 0.02).bfloat16()
+        self.bias = (torch.randn(N, generator=g) * 0.1).bfloat16()
+        self.ptrs = [_upload(lib, L, t) for t in (self.X, self.W, self.bias)]
+        for _ in range(2):
+            p = ctypes.c_void_p()
+            L.check(lib.ojx_malloc(M * N * 2, ctypes.byref(p), None), "ojx_malloc")
+            self.ptrs.append(p.value)
 
-    def desc(c_ptr):
+    def desc(self, out):
+        L = self.L
         d = L.GemmDesc()
-        d.M, d.N, d.K = M, N, K
+        d.M, d.N, d.K = self.M, self.N, self.K
         d.dtype_a = d.dtype_b = d.dtype_c = d.dtype_operand = L.BF16
-        d.trans_b = int(trans_b)
-        d.a, d.b, d.c = px, pw, c_ptr
-        d.operand, d.operand_kind, d.binary_op = pb, L.OPERAND_ROW, L.BINARY["add"]
+        d.trans_b = int(self.trans_b)
+        d.a, d.b, d.c = self.ptrs[0], self.ptrs[1], self.ptrs[3 + out]
+        d.operand, d.operand_kind, d.binary_op = self.ptrs[2], L.OPERAND_ROW, L.BINARY["add"]
         d.n_unary, d.unary[0] = 1, L.UNARY["silu"]
         return d
 
+    def result(self, out) -> torch.Tensor:
+        return _download(self.lib, self.L, self.ptrs[3 + out], (self.M, self.N), torch.bfloat16)
+
+    def oracle(self) -> np.ndarray:
+        return oracle_gemm(self.X, self.W, trans_b=self.trans_b, operand=self.bias, kind="row",
+                           unary=("silu",))
+
+    def free(self):
+        for p in self.ptrs:
+            self.lib.ojx_free(p)
+
+
+# Consecutive problems whose column groups and partial slots overlap: the second
+# reads counters the first left at other counts and slots holding other values.
+PAIRS = [
+    ((16, 14336, 4096, False), (7, 4096, 2048, False)),
+    ((1, 1000, 320, True), (16, 14336, 4096, False)),
+    ((7, 4096, 2048, False), (4, 14336, 4096, True)),
+]
+
+
+@pytest.mark.parametrize("first,second", PAIRS)
+def test_noalloc_two_calls_in_a_row(first, second):
+    lib, L = _lib()
+    probs = [_Problem(lib, L, *first, seed=11), _Problem(lib, L, *second, seed=12)]
     try:
-        L.check(lib.ojx_gemm(ctypes.byref(desc(out[0])), None), "ojx_gemm")
-        assert L.ROUTES[lib.ojx_last_route()] == "skinny"
-        ref = _download(lib, L, out[0], (M, N), torch.bfloat16).float().numpy()
-        for i in (1, 2):  # two calls in a row on the shared scratch array
-            L.check(lib.ojx_gemm_skinny_noalloc(ctypes.byref(desc(out[i])), None), "noalloc")
-            got = _download(lib, L, out[i], (M, N), torch.bfloat16).float().numpy()
-            rel = np.linalg.norm(got - ref) / np.linalg.norm(ref)
-            assert rel <= 4e-3, f"call {i}: rel-L2 {rel:.3e}"
+        regular = []
+        for p in probs:  # the regular entry point (cudaMalloc-grown scratch) first
+            L.check(lib.ojx_gemm(ctypes.byref(p.desc(0)), None), "ojx_gemm")
+            assert L.ROUTES[lib.ojx_last_route()] == "skinny"
+            regular.append(p.result(0))
+        for i, p in enumerate(probs):  # then the no-alloc calls back to back
+            L.check(lib.ojx_gemm_skinny_noalloc(ctypes.byref(p.desc(1)), None), f"noalloc call {i}")
+        for i, p in enumerate(probs):
+            got = p.result(1)
+            assert torch.equal(got.view(torch.int16), regular[i].view(torch.int16)), \
+                f"call {i}: differs from ojx_gemm's skinny route"
+            err = rel_l2(got.float().numpy(), p.oracle())
+            assert err <= 4e-3, f"call {i}: rel-L2 {err:.3e} against the oracle"
     finally:
-        for ptr in [px, pw, pb] + out:
-            lib.ojx_free(ptr)
+        for p in probs:
+            p.free()
 
 
 def test_noalloc_rejects_problems_beyond_its_scratch():
-    import sys
-    import pathlib
-    repo = pathlib.Path(__file__).resolve().parents[1]
-    sys.path[:0] = [str(repo), str(repo / "ojasx-open-source-cuda-_b200")]
-    from torchcl import _lib as L
-
-    lib = L.lib()
-    L.check(lib.ojx_init(0, ctypes.byref(L.DeviceInfo())), "ojx_init")
+    lib, L = _lib()
     p = ctypes.c_void_p()
     L.check(lib.ojx_malloc(1 << 16, ctypes.byref(p), None), "ojx_malloc")
     try:
