@@ -40,7 +40,7 @@ from torchcl.runtime.memory import CLBuffer, get_buffer_pool, note_use
 _opencl_buffers = weakref.WeakValueDictionary()
 _buffer_lock = threading.RLock()
 _tensor_id_counter = 0
-_id_lock = threading.Lock()
+_id_lock = threading.RLock()  # reentrant: a GC finalizer may run while it is held
 
 _NOT_ON_DEVICE = "This tensor is not on the OpenCL device. Use torchcl.to_opencl(tensor) first."
 

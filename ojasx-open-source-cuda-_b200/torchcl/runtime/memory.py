@@ -34,7 +34,7 @@ class CLBuffer:
     __slots__ = ("buffer", "nbytes", "capacity", "dtype", "shape", "_id", "is_pinned", "_freed",
                  "__weakref__")
     _counter = 0
-    _lock = threading.Lock()
+    _lock = threading.RLock()  # reentrant: see CLBufferPool
 
     def __init__(self, buffer: int, nbytes: int, capacity: int, dtype=None, shape=None,
                  is_pinned: bool = False):
@@ -142,7 +142,13 @@ class CLBufferPool:
 
     def __init__(self) -> None:
         self._active: dict[int, CLBuffer] = weakref.WeakValueDictionary()
-        self._lock = threading.Lock()
+        # Reentrant on purpose.  Device-tensor handles return their buffers through
+        # weakref finalizers (torchcl.api), and a finalizer runs wherever a garbage
+        # collection happens to start: possibly on this thread inside one of the
+        # locked sections below (an insertion into _active allocates).  With a plain
+        # Lock, the finalizer's free() would then wait forever for a lock its own
+        # thread holds, a host-side stall with the GPU idle.
+        self._lock = threading.RLock()
 
     def allocate(self, nbytes: int, dtype=None, shape=None, pin_memory: bool = False) -> CLBuffer:
         _ensure_initialized()

@@ -48,3 +48,25 @@ def test_jit_plans_do_not_depend_on_the_element_count():
     assert after["hits"] >= before["hits"] + 1
     with pytest.raises(ValueError):
         jit._plan(None, ["nope"])
+
+
+def test_pool_free_from_a_finalizer_inside_a_locked_section():
+    """A handle's finalizer may run (through a garbage collection) while this thread
+    is inside one of the pool's locked sections; its free() must not wait for the
+    lock its own thread holds."""
+    import threading
+    from torchcl.runtime.memory import CLBuffer, CLBufferPool
+    pool = CLBufferPool()
+    buf = CLBuffer(0, 64, 64)  # a NULL block: ojx_free(NULL) is a no-op
+    done = threading.Event()
+
+    def run():
+        with pool._lock:  # as if a GC fired inside allocate()'s critical section
+            pool.free(buf)
+        done.set()
+
+    t = threading.Thread(target=run, daemon=True)
+    t.start()
+    t.join(timeout=10)
+    assert done.is_set(), "free() inside the pool's own locked section deadlocked"
+    assert buf._freed
