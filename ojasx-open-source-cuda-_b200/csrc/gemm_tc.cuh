@@ -32,6 +32,15 @@ namespace ojx {
 constexpr int TC_BM = 128;
 constexpr int TC_THREADS = 320;  // 2 control warps + 8 epilogue warps
 constexpr int TC_EPI_WARPS = 8;
+// 3xTF32 accumulates each run of TC_TF32_CHUNK_KB k-blocks (256 k) into a fresh
+// TMEM accumulator; the epilogue warps add the runs' sums in registers.  The
+// tensor cores' fp32 accumulation does not round to nearest (it truncates), so
+// one accumulator carried over the whole K collects an error that grows in
+// proportion to K (three MMAs add into it per k-step): measured against the
+// ascending-k fp32 oracle with U(-1,1) operands, rel-L2 1.4e-5 at K = 2048 and
+// 5.7e-5 at K = 8192.  Runs of 256 k bound that part to one run, and the runs
+// are added with IEEE round-to-nearest.
+constexpr int TC_TF32_CHUNK_KB = 8;
 
 // Output tensor maps of the TMA-store epilogue: one per destination buffer.
 struct StoreMaps {
@@ -109,13 +118,10 @@ __device__ __forceinline__ void load_operand(uint32_t dst, const CUtensorMap* ma
   }
 }
 
-// Epilogue for 16 consecutive columns of one output row.
-__device__ __forceinline__ void store_row16(const EpiParams& ep, const uint32_t (&r)[16],
-                                            int64_t row, int col0, int N) {
-  float v[16];
+// Epilogue for 16 consecutive columns of one output row (accumulator values in v).
+__device__ __forceinline__ void store_row16f(const EpiParams& ep, float (&v)[16], int64_t row,
+                                             int col0, int N) {
   const int valid = min(16, N - col0);
-#pragma unroll
-  for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
   epilogue16(ep, v, row, col0, valid);
   const int esz = ep.dtype_c == OJX_F32 ? 4 : 2;
   const int64_t off = (row * ep.ldc + ep.col_offset + col0) * esz;
@@ -155,26 +161,26 @@ __device__ __forceinline__ void store_row16(const EpiParams& ep, const uint32_t 
     }
   }
 }
+__device__ __forceinline__ void store_row16(const EpiParams& ep, const uint32_t (&r)[16],
+                                            int64_t row, int col0, int N) {
+  float v[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
+  store_row16f(ep, v, row, col0, N);
+}
 
-// TMA-store epilogue of one 128-byte-wide chunk of a warp's 32 rows: TMEM ->
-// registers -> epilogue -> packed values in the warp's swizzled staging box ->
-// one tensor store per destination.  ESZ = output element bytes (chunk = 128/ESZ
-// columns).  `tcol` is the chunk's first TMEM column, `col0` its first output
-// column (relative to the destination maps), `row0` the box's first row.
+// TMA-store epilogue of one 128-byte-wide chunk of a warp's 32 rows: accumulator
+// values -> epilogue -> packed values in the warp's swizzled staging box -> one
+// tensor store per destination.  ESZ = output element bytes (chunk = 128/ESZ
+// columns); `col0` is the chunk's first output column (relative to the
+// destination maps), `row0` the box's first row.  epi_chunk_tma_regs takes the
+// values in registers, epi_chunk_tma reads them from TMEM columns tcol...
 template <int ESZ, int BATCH>
-__device__ __forceinline__ void epi_chunk_tma(const EpiParams& ep, const StoreMaps& maps,
-                                              uint32_t tcol, int64_t row, int M, int col0, int N,
-                                              uint32_t stage, int lane, int row0, int bidx) {
+__device__ __forceinline__ void epi_chunk_tma_regs(const EpiParams& ep, const StoreMaps& maps,
+                                                   float (&v)[128 / ESZ], int64_t row, int M,
+                                                   int col0, int N, uint32_t stage, int lane,
+                                                   int row0, int bidx) {
   constexpr int V = 128 / ESZ;
-  float v[V];
-#pragma unroll
-  for (int i = 0; i < V / 16; ++i) {
-    uint32_t r[16];
-    tmem_ld16(tcol + i * 16, r);
-    tmem_wait_ld();
-#pragma unroll
-    for (int j = 0; j < 16; ++j) v[i * 16 + j] = __uint_as_float(r[j]);
-  }
 #pragma unroll
   for (int i = 0; i < V / 16; ++i) {
     float w[16];
@@ -227,6 +233,22 @@ __device__ __forceinline__ void epi_chunk_tma(const EpiParams& ep, const StoreMa
     }
     bulk_commit_group();
   }
+}
+template <int ESZ, int BATCH>
+__device__ __forceinline__ void epi_chunk_tma(const EpiParams& ep, const StoreMaps& maps,
+                                              uint32_t tcol, int64_t row, int M, int col0, int N,
+                                              uint32_t stage, int lane, int row0, int bidx) {
+  constexpr int V = 128 / ESZ;
+  float v[V];
+#pragma unroll
+  for (int i = 0; i < V / 16; ++i) {
+    uint32_t r[16];
+    tmem_ld16(tcol + i * 16, r);
+    tmem_wait_ld();
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[i * 16 + j] = __uint_as_float(r[j]);
+  }
+  epi_chunk_tma_regs<ESZ, BATCH>(ep, maps, v, row, M, col0, N, stage, lane, row0, bidx);
 }
 
 template <int KIND, int FMT, int A_MN, int B_MN, int BN, int STAGES, int STORE_TMA, int BATCH = 0>
@@ -340,43 +362,52 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       int stage = 0, acc = 0;
       uint32_t phase = 0, acc_phase = 0;
       bool ok = true;
+      // Each run of KCH k-blocks goes into one TMEM accumulator buffer (KIND 0: the
+      // whole K, one run per tile; 3xTF32: runs of TC_TF32_CHUNK_KB, see above).
+      const int KCH = KIND == 1 ? TC_TF32_CHUNK_KB : KB;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, budget, s_abort)) break;
-        tc_fence_after();
-        const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
-        for (int kb = 0; kb < KB; ++kb) {
-          if (!mbar_wait(full_bar(stage), phase, budget, s_abort)) {
+        for (int kc = 0; kc < KB && ok; kc += KCH) {
+          if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, budget, s_abort)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t sA = sbase + stage * L::STAGE_BYTES;
-          const uint32_t sB = sA + L::A_BYTES;
+          const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
+          const int kend = min(KB, kc + KCH);
+          for (int kb = kc; kb < kend; ++kb) {
+            if (!mbar_wait(full_bar(stage), phase, budget, s_abort)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t sA = sbase + stage * L::STAGE_BYTES;
+            const uint32_t sB = sA + L::A_BYTES;
 #pragma unroll
-          for (int ks = 0; ks < 4; ++ks) {
-            const uint64_t ad = operand_desc<A_MN, L::BK>(sA, ks);
-            const uint64_t bd = operand_desc<B_MN, L::BK>(sB, ks);
-            const uint32_t accum = (kb | ks) != 0 ? 1u : 0u;
-            if (KIND == 0) {
-              mma_f16(d, ad, bd, IDESC, accum);
-            } else {
-              const uint64_t ad_lo = operand_desc<A_MN, L::BK>(sB + L::B_BYTES, ks);
-              const uint64_t bd_lo = operand_desc<B_MN, L::BK>(sB + L::B_BYTES + L::A_BYTES, ks);
-              mma_tf32(d, ad_lo, bd, IDESC, accum);  // Al * Bh
-              mma_tf32(d, ad, bd_lo, IDESC, 1u);     // Ah * Bl
-              mma_tf32(d, ad, bd, IDESC, 1u);        // Ah * Bh
+            for (int ks = 0; ks < 4; ++ks) {
+              const uint64_t ad = operand_desc<A_MN, L::BK>(sA, ks);
+              const uint64_t bd = operand_desc<B_MN, L::BK>(sB, ks);
+              const uint32_t accum = (kb != kc || ks != 0) ? 1u : 0u;
+              if (KIND == 0) {
+                mma_f16(d, ad, bd, IDESC, accum);
+              } else {
+                const uint64_t ad_lo = operand_desc<A_MN, L::BK>(sB + L::B_BYTES, ks);
+                const uint64_t bd_lo = operand_desc<B_MN, L::BK>(sB + L::B_BYTES + L::A_BYTES, ks);
+                mma_tf32(d, ad_lo, bd, IDESC, accum);  // Al * Bh
+                mma_tf32(d, ad, bd_lo, IDESC, 1u);     // Ah * Bl
+                mma_tf32(d, ad, bd, IDESC, 1u);        // Ah * Bh
+              }
+            }
+            mma_commit(empty_bar(stage));  // smem slot free once these MMAs have read it
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1u;
             }
           }
-          mma_commit(empty_bar(stage));  // smem slot free once these MMAs have read it
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1u;
-          }
+          if (!ok) break;
+          mma_commit(tfull_bar(acc));  // this run's sum ready for the epilogue
+          acc ^= 1;
+          if (acc == 0) acc_phase ^= 1u;
         }
-        if (!ok) break;
-        mma_commit(tfull_bar(acc));  // accumulator ready for the epilogue
-        acc ^= 1;
-        if (acc == 0) acc_phase ^= 1u;
       }
       // Every MMA issued above must complete before TMEM is released.
       mma_commit(done_bar);
@@ -389,7 +420,92 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const int half = (warp - 2) >> 2;
     int acc = 0;
     uint32_t acc_phase = 0;
+    // 3xTF32: the tile's K arrives as runs of TC_TF32_CHUNK_KB k-blocks, each in one
+    // TMEM buffer.  This warp adds its 32 rows x BN/2 columns of every run into
+    // registers (fp32, round to nearest) and frees the buffer at once; after the
+    // last run it applies the epilogue to the sums and stores them.  Returns false
+    // when a bounded wait gave up.
+    auto epi_tile_runs = [&](int tile) -> bool {
+      constexpr int HC = BN / 2;
+      float sum[HC];
+      const int KCH = TC_TF32_CHUNK_KB;
+      for (int kc = 0; kc < KB; kc += KCH) {
+        if (!mbar_wait(tfull_bar(acc), acc_phase, budget, s_abort)) return false;
+        tc_fence_after();
+        const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                            static_cast<uint32_t>(acc * BN + half * HC);
+#pragma unroll
+        for (int i = 0; i < HC; i += 16) {
+          uint32_t r[16];
+          tmem_ld16(tb + i, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            sum[i + j] = kc == 0 ? __uint_as_float(r[j]) : sum[i + j] + __uint_as_float(r[j]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(tempty_bar(acc));
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+      const int bidx = BATCH ? tile / tiles_per : 0;
+      int mb, nb;
+      tile_coords(tile - bidx * tiles_per, tiles_m, tiles_n, mb, nb);
+      EpiParams epb = ep;
+      if (BATCH) {
+        const int esz_c = ep.dtype_c == OJX_F32 ? 4 : 2;
+        const int esz_o = ep.dtype_operand == OJX_F32 ? 4 : 2;
+        epb.dst[0] = static_cast<char*>(ep.dst[0]) + bidx * bp.stride_c * esz_c;
+        if (ep.operand)
+          epb.operand = static_cast<const char*>(ep.operand) + bidx * bp.stride_op * esz_o;
+      }
+      const int64_t row = static_cast<int64_t>(mb) * TC_BM + q * 32 + lane;
+      const int n0 = nb * BN + half * HC;
+      if (STORE_TMA) {
+        const uint32_t stage_box = sout + static_cast<uint32_t>((warp - 2) * L::STAGE_OUT_BYTES);
+        const int row0 = mb * TC_BM + q * 32;
+        if (ep.dtype_c == OJX_F32) {
+#pragma unroll
+          for (int c = 0; c < HC; c += 32) {
+            if (n0 + c < N) {
+              float v[32];
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = sum[c + j];
+              epi_chunk_tma_regs<4, BATCH>(epb, smaps, v, row, M, n0 + c, N, stage_box, lane, row0,
+                                           bidx);
+            }
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < HC; c += 64) {
+            if (n0 + c < N) {
+              float v[64];
+#pragma unroll
+              for (int j = 0; j < 64; ++j) v[j] = sum[c + j];
+              epi_chunk_tma_regs<2, BATCH>(epb, smaps, v, row, M, n0 + c, N, stage_box, lane, row0,
+                                           bidx);
+            }
+          }
+        }
+      } else if (row < M) {
+#pragma unroll
+        for (int c = 0; c < HC; c += 16) {
+          if (n0 + c < N) {
+            float v[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = sum[c + j];
+            store_row16f(epb, v, row, n0 + c, N);
+          }
+        }
+      }
+      return true;
+    };
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      if (KIND == 1) {
+        if (!epi_tile_runs(tile)) break;
+        continue;
+      }
       if (!mbar_wait(tfull_bar(acc), acc_phase, budget, s_abort)) break;
       tc_fence_after();
       const int bidx = BATCH ? tile / tiles_per : 0;
