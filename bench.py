@@ -394,9 +394,14 @@ def run_ours(args, cfg, world, rank, local):
     flops_total = 2.0 * M * N * K
     value = flops_total * args.steps / (total_ms / 1e3) / 1e12
 
+    breakdown = None
+    if world > 1 and args.gather == "p2p":
+        breakdown = _sharded_breakdown(args, lib, L, d, A, Ws, biases, n_copies, M, Nl, ev, gemm_ms,
+                                       dev, stream, world, sharded, cfg["act"])
+
     # e2e through the C-ABI with pinned host buffers
-    e2e = e2e_measure(args, lib, L, A, C, M, K, N, es, gemm, gather, world, dev, stream,
-                      desc=d if sharded is None else None)
+    e2e = e2e_measure(args, lib, L, A, C, M, K, N, es, gemm, gather, world, dev, stream, cfg=cfg,
+                      W=Ws[0], bias=biases[0])
 
     peaks, peak_kind = _peaks()
     avg_gemm_ms = statistics.mean(gemm_ms)
@@ -443,6 +448,8 @@ def run_ours(args, cfg, world, rank, local):
                 "clock_samples": clocks.get("samples"), "power_w_max": clocks.get("power_w_max")}
         if graph is not None:
             line["graph"] = graph
+        if breakdown is not None:
+            line["step_breakdown"] = breakdown
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
@@ -452,63 +459,135 @@ def run_ours(args, cfg, world, rank, local):
     return 0
 
 
-def e2e_measure(args, lib, L, A, C, M, K, N, es, gemm, gather, world, dev, stream, desc=None):
-    """Same metric end to end: pinned host A -> device, GEMM (+gather), C -> pinned host.
-    On one GPU through ojx_gemm_host_io (chunks of rows: uploads, GEMMs and downloads
-    overlap on three streams); on several, upload, sharded GEMM with the gather, barrier
-    and download one after another."""
+def _sharded_breakdown(args, lib, L, d, A, Ws, biases, n_copies, M, Nl, ev, gemm_ms, dev, stream,
+                       world, sharded, act):
+    """Where a sharded step's time goes, max over ranks (all ranks take part).
+
+    After the timed steps, `args.steps` pairs of launches alternate on each rank:
+    the all-gathering GEMM (its epilogue stores every tile into all ranks' C; the
+    kernel completes after its stores and a system-scope fence) and the same GEMM
+    writing only this rank's [M, N/P] block.  Alternating them keeps both under the
+    same clock and power state; their mean difference is the peer-store tail.  The
+    completion barrier (the one-element all-reduce after the kernel) is taken from
+    the timed steps."""
+    import torch
+    import torch.distributed as dist
+    barrier_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in ev)
+    C_local = torch.empty(M, Nl, device=dev, dtype=A.dtype)
+    dl = L.GemmDesc.from_buffer_copy(d)
+    dl.c, dl.ldc = C_local.data_ptr(), Nl
+    sp = stream.cuda_stream
+    pairs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    torch.cuda._sleep(int(1e6 + 2e5 * args.steps))
+    for i, e in enumerate(pairs):
+        w, b = Ws[i % n_copies].data_ptr(), biases[i % n_copies].data_ptr()
+        dl.b, dl.operand = w, b
+        e[0].record(stream)
+        L.check(lib.ojx_gemm(ctypes.byref(dl), sp), "local gemm")
+        e[1].record(stream)
+        sharded.launch(A.data_ptr(), w, b, (act,))
+        e[2].record(stream)
+        sharded.barrier()
+        e[3].record(stream)
+    torch.cuda.synchronize(dev)
+    local_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in pairs)
+    ag_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in pairs)
+    t = torch.tensor([statistics.mean(gemm_ms), ag_ms, local_ms, barrier_ms], device=dev,
+                     dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    timed, ag, loc, bar = (float(x) for x in t.tolist())
+    del C_local
+    return {"gemm_allgather_ms": timed, "pairs_allgather_ms": ag, "pairs_local_only_ms": loc,
+            "peer_store_tail_ms": ag - loc, "completion_barrier_ms": bar,
+            "note": "per step, max over ranks; pairs_*: all-gathering and local-only launches of the "
+                    "same GEMM alternated after the timed steps"}
+
+
+def e2e_measure(args, lib, L, A, C, M, K, N, es, gemm, gather, world, dev, stream, cfg=None,
+                W=None, bias=None):
+    """Same metric end to end, host memory in and out, every step.
+
+    One GPU: through the public torchcl API, as a user of the reference writes it:
+    to_opencl(A) of a pinned host A, the lazy act(add(matmul(a, w), b)) and to_cpu,
+    which runs the upload, the fused GEMM and the download as one overlapped
+    pipeline (ojx_gemm_host_io) and returns C in pinned host memory; W and the bias
+    stay resident.  Several GPUs: through the C-ABI and the mesh, upload, sharded
+    GEMM with the gather, barrier and download one after another.  CUDA events on
+    the stream the work runs on; max over ranks."""
     import torch
     import torch.distributed as dist
     a_bytes = M * K * es
     c_bytes = M * N * es
-    ha, hc = ctypes.c_void_p(), ctypes.c_void_p()
-    L.check(lib.ojx_host_alloc(a_bytes, ctypes.byref(ha)), "pinned A")
-    L.check(lib.ojx_host_alloc(c_bytes, ctypes.byref(hc)), "pinned C")
-    sp = stream.cuda_stream
-    # host copy of this step's input
-    L.check(lib.ojx_memcpy_d2h(ha.value, A.data_ptr(), a_bytes, sp))
-    torch.cuda.synchronize(dev)
-
-    if desc is not None:
-        dh = L.GemmDesc.from_buffer_copy(desc)
-        dh.a, dh.c = ha.value, hc.value
+    if world == 1:
+        import torchcl
+        from torchcl.runtime.context import get_queue
+        torchcl.init_opencl(device_index=dev.index or 0)
+        A_host = A.cpu().pin_memory()
+        w, b = torchcl.to_opencl(W.cpu()), torchcl.to_opencl(bias.cpu())
+        act = getattr(torchcl, cfg["act"])
+        qstream = torch.cuda.ExternalStream(get_queue(), device=dev)
+        holder = []
 
         def step():
-            L.check(lib.ojx_gemm_host_io(ctypes.byref(dh), A.data_ptr(), C.data_ptr(), 0, sp),
-                    "gemm_host_io")
+            a = torchcl.to_opencl(A_host)
+            holder[:] = [torchcl.to_cpu(act(torchcl.add(torchcl.matmul(a, w), b)))]
+        estream = qstream
     else:
+        ha, hc = ctypes.c_void_p(), ctypes.c_void_p()
+        L.check(lib.ojx_host_alloc(a_bytes, ctypes.byref(ha)), "pinned A")
+        L.check(lib.ojx_host_alloc(c_bytes, ctypes.byref(hc)), "pinned C")
+        sp = stream.cuda_stream
+        L.check(lib.ojx_memcpy_d2h(ha.value, A.data_ptr(), a_bytes, sp))
+        torch.cuda.synchronize(dev)
+
         def step():
             L.check(lib.ojx_memcpy_h2d(A.data_ptr(), ha.value, a_bytes, sp), "h2d")
             gemm()
             gather()
             L.check(lib.ojx_memcpy_d2h(hc.value, C.data_ptr(), c_bytes, sp), "d2h")
+        estream = stream
 
+    # Untimed warm-up steps, at least two: a caller keeps the previous result while
+    # the next step runs, so the pinned-memory cache settles on two output blocks
+    # (the first allocation of a 2 GB pinned block costs the better part of a second).
     steps = max(2, args.steps)
-    step()
+    for _ in range(max(2, args.warmup)):
+        step()
     torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
+    e0.record(estream)
     for _ in range(steps):
         step()
-    e1.record(stream)
+    e1.record(estream)
     torch.cuda.synchronize(dev)
     dt = e0.elapsed_time(e1) / 1e3
     t = torch.tensor([dt], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     dt = float(t.item())
-    lib.ojx_host_free(ha.value)
-    lib.ojx_host_free(hc.value)
+    if world == 1:
+        ok = bool(torch.equal(holder[0].view(-1)[:1 << 20].to(dev), C.view(-1)[:1 << 20]))
+        holder.clear()
+        note = ("torchcl public API: to_opencl(pinned A) -> " + cfg["act"] + "(add(matmul(a, w), b))"
+                " -> to_cpu, which overlaps the chunked upload, fused GEMM and download "
+                "(ojx_gemm_host_io); W and bias resident")
+    else:
+        lib.ojx_host_free(ha.value)
+        lib.ojx_host_free(hc.value)
+        ok = None
+        note = "C-ABI with pinned host buffers: upload, GEMM + gather, download; max over ranks"
     flops = 2.0 * M * N * K * steps
-    return {"value": flops / dt / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": a_bytes,
-            "d2h_bytes_per_step": c_bytes, "steps": steps,
-            "note": ("ojx_gemm_host_io (C-ABI, pinned host A and C, chunked: copies overlap the GEMM)"
-                     if desc is not None else
-                     "C-ABI with pinned host buffers: upload, GEMM + gather, download; max over ranks")
-            + "; CUDA events on the launching stream"}
+    out = {"value": flops / dt / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": a_bytes,
+           "d2h_bytes_per_step": c_bytes, "steps": steps,
+           "note": note + "; CUDA events on the stream the work runs on"}
+    if ok is not None:
+        out["matches_device_run"] = ok
+    return out
 
 
 def run_train(args, cfg):

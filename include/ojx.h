@@ -28,6 +28,7 @@ extern "C" {
  * OJX_ERR_OOM      -> MemoryError  (after evict-and-retry, torchcl/runtime/memory.py:109-115)
  * OJX_ERR_TIMEOUT  -> RuntimeError (a bounded device-side wait expired; the kernel returned)
  * OJX_ERR_CUDA     -> RuntimeError (any CUDA runtime/driver failure)
+ * OJX_ERR_BOUNDS   -> RuntimeError (bounds-checking build only: a device-side check failed)
  */
 enum {
   OJX_OK = 0,
@@ -36,7 +37,8 @@ enum {
   OJX_ERR_CUDA = 3,
   OJX_ERR_TIMEOUT = 4,
   OJX_ERR_UNSUPPORTED = 5,
-  OJX_ERR_NOT_INITIALIZED = 6
+  OJX_ERR_NOT_INITIALIZED = 6,
+  OJX_ERR_BOUNDS = 7
 };
 
 /* element types */
@@ -158,6 +160,13 @@ int ojx_current_device(int* device);
 int ojx_synchronize(void);                               /* context.py:143-146 synchronize */
 const char* ojx_last_error(void);                        /* thread-local message of the last failure */
 int ojx_poll_device_error(void);                         /* reads and clears the kernels' error word */
+/* 1 in the bounds-checking build (libojx_debug.so, compiled with OJX_DEBUG_BOUNDS), else 0.
+ * That build checks every TMA tile origin and epilogue store of the GEMM and attention
+ * kernels on the device; a failed check skips the access, and the next
+ * ojx_poll_device_error returns OJX_ERR_BOUNDS with the site and coordinates.  No
+ * counterpart in the reference (which has no device-side checks); it serves the
+ * sanitizer role of compute-sanitizer, which this library's tests do not rely on. */
+int ojx_debug_bounds_enabled(void);
 int ojx_set_wait_budget(uint64_t cycles);                /* bound of every device-side spin wait */
 uint64_t ojx_kernel_launch_count(void);                  /* kernels this library launched so far */
 int ojx_last_route(void);                                /* OJX_ROUTE_* of this thread's last ojx_gemm */

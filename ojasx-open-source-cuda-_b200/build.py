@@ -1,4 +1,5 @@
-"""Build libojx.so (the sm_100a kernels + C-ABI runtime) in-tree.
+"""Build libojx.so (the sm_100a kernels + C-ABI runtime) in-tree, and its
+bounds-checking twin libojx_debug.so (-DOJX_DEBUG_BOUNDS).
 
     python ojasx-open-source-cuda-_b200/build.py [--verbose-ptxas]
 
@@ -37,40 +38,57 @@ def nvcc() -> str:
     raise RuntimeError("nvcc not found")
 
 
-def _compile(src: str, verbose_ptxas: bool) -> pathlib.Path:
-    obj = OBJ_DIR / (pathlib.Path(src).stem + ".o")
-    cmd = [nvcc(), *ARCH, *COMMON, "-c", str(CSRC / src), "-o", str(obj)]
+# Two builds of the same sources: the library itself, and the bounds-checking build
+# (every TMA tile origin and epilogue store checked on the device; torchcl loads it
+# when OJX_DEBUG_BOUNDS=1).
+VARIANTS = {"release": (LIB, OBJ_DIR, []),
+            "debug": (OUT_DIR / "libojx_debug.so", OBJ_DIR / "debug", ["-DOJX_DEBUG_BOUNDS"])}
+
+
+def _compile(src: str, obj_dir: pathlib.Path, defs: list[str], verbose_ptxas: bool) -> pathlib.Path:
+    obj = obj_dir / (pathlib.Path(src).stem + ".o")
+    cmd = [nvcc(), *ARCH, *COMMON, *defs, "-c", str(CSRC / src), "-o", str(obj)]
     if verbose_ptxas and src.endswith(".cu"):
         cmd += ["-Xptxas", "-v"]
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
         raise RuntimeError(f"nvcc failed for {src}:\n{res.stdout}\n{res.stderr}")
     if verbose_ptxas and res.stderr:
-        (OBJ_DIR / (pathlib.Path(src).stem + ".ptxas.txt")).write_text(res.stderr)
+        (obj_dir / (pathlib.Path(src).stem + ".ptxas.txt")).write_text(res.stderr)
     return obj
 
 
-def _stale() -> bool:
-    if not LIB.exists():
+def _stale(lib: pathlib.Path) -> bool:
+    if not lib.exists():
         return True
-    t = LIB.stat().st_mtime
+    t = lib.stat().st_mtime
     deps = list(CSRC.glob("*")) + list(INCLUDE.glob("*.h")) + [pathlib.Path(__file__)]
     return any(p.stat().st_mtime > t for p in deps)
 
 
-def build(force: bool = False, verbose_ptxas: bool = False) -> pathlib.Path:
-    if not force and not _stale():
-        return LIB
-    OBJ_DIR.mkdir(parents=True, exist_ok=True)
-    OUT_DIR.mkdir(parents=True, exist_ok=True)
-    with cf.ThreadPoolExecutor(max_workers=len(SOURCES)) as ex:
-        objs = list(ex.map(lambda s: _compile(s, verbose_ptxas), SOURCES))
-    tmp = LIB.with_suffix(".so.tmp")
+def _link(lib: pathlib.Path, objs: list[pathlib.Path]) -> None:
+    tmp = lib.with_suffix(".so.tmp")
     cmd = [nvcc(), *ARCH, "-shared", "-o", str(tmp), *map(str, objs), "-ldl"]
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
         raise RuntimeError(f"link failed:\n{res.stdout}\n{res.stderr}")
-    os.replace(tmp, LIB)
+    os.replace(tmp, lib)
+
+
+def build(force: bool = False, verbose_ptxas: bool = False) -> pathlib.Path:
+    """Build every stale variant (both compile in parallel); returns the release library."""
+    todo = {name: v for name, v in VARIANTS.items() if force or _stale(v[0])}
+    if not todo:
+        return LIB
+    OUT_DIR.mkdir(parents=True, exist_ok=True)
+    jobs = []
+    for name, (lib, obj_dir, defs) in todo.items():
+        obj_dir.mkdir(parents=True, exist_ok=True)
+        jobs += [(name, src, obj_dir, defs) for src in SOURCES]
+    with cf.ThreadPoolExecutor(max_workers=len(jobs)) as ex:
+        objs = list(ex.map(lambda j: (j[0], _compile(j[1], j[2], j[3], verbose_ptxas)), jobs))
+    for name, (lib, _, _) in todo.items():
+        _link(lib, [o for n, o in objs if n == name])
     return LIB
 
 

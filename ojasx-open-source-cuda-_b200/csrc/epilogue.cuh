@@ -17,6 +17,7 @@
 #include <cuda_fp16.h>
 #include <cstdint>
 #include "../../include/ojx.h"
+#include "sm100.cuh"
 
 namespace ojx {
 
@@ -88,7 +89,19 @@ struct EpiParams {
   int32_t n_dst;
   int64_t col_offset;
   void* dst[OJX_MAX_PEERS];
+  // Logical output extent [m_rows, n_cols] (stores land at row < m_rows, col <
+  // n_cols); read only by the debug build's bounds checks.
+  int64_t m_rows;
+  int64_t n_cols;
 };
+
+// Debug build: a store of n values at (row, col .. col+n-1) lies inside the output.
+__device__ __forceinline__ bool epi_store_ok(const EpiParams& ep, int site, int64_t row,
+                                             int64_t col, int n) {
+  if (!kDebugBounds) return true;
+  const bool ok = row >= 0 && col >= 0 && row < ep.m_rows && col + n <= ep.n_cols;
+  return bounds_check(ok, site, row, col, row < ep.m_rows ? ep.n_cols : ep.m_rows);
+}
 
 struct Dests;
 // Host: copy the epilogue fields of a GEMM descriptor (and the destinations of an

@@ -138,7 +138,10 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       if (is_k) {
         mbar_arrive_expect_tx(q_full, L::Q_BYTES);
 #pragma unroll
-        for (int db = 0; db < L::DB; ++db) tma_load_3d(sQ + db * 16384, &tmQ, q_full, db * 64, q0, bh);
+        for (int db = 0; db < L::DB; ++db)
+          if (tma_origin_ok(SITE_FA_LOAD, db * 64, q0, D, p.M, 2) &&
+              bounds_check(bh < p.BH, SITE_FA_LOAD, bh, q0, p.BH))
+            tma_load_3d(sQ + db * 16384, &tmQ, q_full, db * 64, q0, bh);
       }
       for (int j = 0; j < kv_tiles; ++j) {
         const int st = j % FA_ST;
@@ -149,12 +152,15 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
           mbar_arrive_expect_tx(k_full(st), L::K_BYTES);
 #pragma unroll
           for (int db = 0; db < L::DB; ++db)
-            tma_load_3d(sK + db * 16384, &tmK, k_full(st), db * 64, j * FA_BN, bh);
+            if (tma_origin_ok(SITE_FA_LOAD, db * 64, j * FA_BN, D, p.nk, 2))
+              tma_load_3d(sK + db * 16384, &tmK, k_full(st), db * 64, j * FA_BN, bh);
         } else {
           if (!mbar_wait(v_empty(st), ph ^ 1u, p.budget, s_abort)) break;
           mbar_arrive_expect_tx(v_full(st), L::V_BYTES);
+          // (the second 64-key box of a ragged last tile may start past the keys)
+          const int v_boxes = tma_origin_ok(SITE_FA_LOAD, 0, j * FA_BN, D, p.nk, 2) ? 2 : 0;
 #pragma unroll
-          for (int kb = 0; kb < 2; ++kb)
+          for (int kb = 0; kb < v_boxes; ++kb)
 #pragma unroll
             for (int db = 0; db < L::DB; ++db)
               tma_load_3d(sV + (kb * L::DB + db) * 8192, &tmV, v_full(st), db * 64,
@@ -372,7 +378,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
             pk[i / 2] = *reinterpret_cast<const uint32_t*>(&h);
           }
         }
-        if (qi < p.M) {
+        if (qi < p.M && bounds_check(c + 16 <= D && bh < p.BH, SITE_FA_STORE, qi, c, D)) {
           uint4* d4 = reinterpret_cast<uint4*>(dst + c * 2);
           d4[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
           d4[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);

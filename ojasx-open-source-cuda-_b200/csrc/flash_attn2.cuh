@@ -147,8 +147,13 @@ __global__ void __launch_bounds__(F2_THREADS, 1)
       uint32_t issued = 0, issued_parity = 0;
       if (is_k) {
         mbar_arrive_expect_tx(q_full, F2_QT * L::QT_BYTES);
+        // (tile 0 must start inside Q; tile 1 of a ragged last block may start past M)
+        const int q_loads = tma_origin_ok(SITE_FA_LOAD, 0, q0, D, p.M, 2) &&
+                                    bounds_check(bh < p.BH, SITE_FA_LOAD, bh, q0, p.BH)
+                                ? F2_QT
+                                : 0;
 #pragma unroll
-        for (int t = 0; t < F2_QT; ++t)
+        for (int t = 0; t < q_loads; ++t)
 #pragma unroll
           for (int db = 0; db < L::DB; ++db)
             tma_load_3d(sQ + t * L::QT_BYTES + db * 16384, &tmQ, q_full, db * 64, q0 + t * F2_BM, bh);
@@ -163,13 +168,16 @@ __global__ void __launch_bounds__(F2_THREADS, 1)
           mbar_arrive_expect_tx(k_full(st), L::K_BYTES);
 #pragma unroll
           for (int db = 0; db < L::DB; ++db)
-            tma_load_3d(sK + db * 16384, &tmK, k_full(st), db * 64, j * F2_BN, bh);
+            if (tma_origin_ok(SITE_FA_LOAD, db * 64, j * F2_BN, D, p.nk, 2))
+              tma_load_3d(sK + db * 16384, &tmK, k_full(st), db * 64, j * F2_BN, bh);
         } else {
           const uint32_t sV = sV0 + st * L::V_BYTES;
           if (!mbar_wait(v_empty(st), ph ^ 1u, p.budget, s_abort)) break;
           mbar_arrive_expect_tx(v_full(st), L::V_BYTES);
+          // (the second 64-key box of a ragged last tile may start past the keys)
+          const int v_boxes = tma_origin_ok(SITE_FA_LOAD, 0, j * F2_BN, D, p.nk, 2) ? 2 : 0;
 #pragma unroll
-          for (int kb = 0; kb < 2; ++kb)
+          for (int kb = 0; kb < v_boxes; ++kb)
 #pragma unroll
             for (int db = 0; db < L::DB; ++db)
               tma_load_3d(sV + (kb * L::DB + db) * 8192, &tmV, v_full(st), db * 64,
@@ -399,7 +407,7 @@ __global__ void __launch_bounds__(F2_THREADS, 1)
             pk[i / 2] = *reinterpret_cast<const uint32_t*>(&h);
           }
         }
-        if (qi < p.M) {
+        if (qi < p.M && bounds_check(c + 16 <= D && bh < p.BH, SITE_FA_STORE, qi, c, D)) {
           uint4* d4 = reinterpret_cast<uint4*>(dst + c * 2);
           d4[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
           d4[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);

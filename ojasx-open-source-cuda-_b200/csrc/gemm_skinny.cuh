@@ -188,6 +188,11 @@ __global__ void __launch_bounds__(SK_THREADS, 2)
     if (lane == 0 && !p.silence_producer) {
       auto load_w = [&](uint32_t sW, uint32_t fb, int g, int kb) {
         const int n0 = g * (SK_TPU * SK_BN), k0 = kb * SK_BK;
+        // (the unit's first box must start inside W; the others of a ragged last group
+        // may start past N and read the zero fill)
+        if (W_MN ? !tma_origin_ok(SITE_SK_LOAD_W, n0, k0, p.N, p.K, 2)
+                 : !tma_origin_ok(SITE_SK_LOAD_W, k0, n0, p.K, p.N, 2))
+          return;
 #pragma unroll
         for (int j = 0; j < SK_TPU; ++j) {
           if (W_MN) {
@@ -218,7 +223,8 @@ __global__ void __launch_bounds__(SK_THREADS, 2)
       long long u = u_first;
       uint32_t phase = 0, issued = 0, issued_parity = 0;
       for (int i = 0; i < n_early; ++i) {  // X of the units whose W is already on its way
-        tma_load_2d(sbase + i * SK_STAGE_BYTES + SK_W_BYTES, &tmX, full_bar(i), kb * SK_BK, 0);
+        if (tma_origin_ok(SITE_SK_LOAD_X, kb * SK_BK, 0, p.K, p.M, 2))
+          tma_load_2d(sbase + i * SK_STAGE_BYTES + SK_W_BYTES, &tmX, full_bar(i), kb * SK_BK, 0);
         issued |= 1u << i;
         advance(u, g, kb, 1);
       }
@@ -230,7 +236,8 @@ __global__ void __launch_bounds__(SK_THREADS, 2)
         mbar_arrive_expect_tx(fb, SK_STAGE_BYTES);
         const uint32_t sW = sbase + stage * SK_STAGE_BYTES;
         load_w(sW, fb, g, kb);
-        tma_load_2d(sW + SK_W_BYTES, &tmX, fb, kb * SK_BK, 0);
+        if (tma_origin_ok(SITE_SK_LOAD_X, kb * SK_BK, 0, p.K, p.M, 2))
+          tma_load_2d(sW + SK_W_BYTES, &tmX, fb, kb * SK_BK, 0);
         issued |= 1u << stage;
         issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
         if (++stage == SK_STAGES) {
@@ -410,7 +417,7 @@ __global__ void __launch_bounds__(SK_THREADS, 2)
                 mbar_arrive_expect_tx(red_bar, static_cast<uint32_t>((ncontrib - 1) * SK_TPU * p.M * 512));
                 const float* gb = p.partials + static_cast<long long>(g) * p.maxc * SK_SLOT;
                 for (int jj = 0; jj < ncontrib; ++jj) {
-                  if (jj == jc) continue;
+                  if (jj == jc || !bounds_check(jj < p.maxc, SITE_SK_SLOT, g, jj, p.maxc)) continue;
 #pragma unroll
                   for (int j = 0; j < SK_TPU; ++j)
                     bulk_load_g2s(sbase + static_cast<uint32_t>(((jj * SK_TPU + j) * p.M) * 512),
@@ -535,7 +542,7 @@ __global__ void __launch_bounds__(SK_THREADS, 2)
               if (ep.operand_kind != OJX_OPERAND_NONE)
                 binary_n<8>(ep.binary_op, ep.operand_is_lhs != 0, y, x);
               for (int i = 0; i < ep.n_unary; ++i) unary_n_half<8>(unary_at(ep.unary_packed, i), y);
-              if (!warm) {
+              if (!warm && epi_store_ok(ep, SITE_SK_STORE, m, fn, fvalid)) {
 #pragma unroll
                 for (int di = 0; di < OJX_MAX_PEERS; ++di) {
                   if (di >= ep.n_dst) break;

@@ -99,9 +99,17 @@ __device__ __forceinline__ uint64_t operand_desc(uint32_t base, int ks) {
 }
 
 // Loads of one operand tile (rows = 128 for A, BN for B) at (mn0, k0) of matrix bc.
+// ext_mn / ext_k: the operand's extents (debug bounds checks only; the tile origin
+// must lie inside, further 64-wide MN boxes of a partial tile may start past the
+// edge and read the zero fill).
 template <int MN, int BK, int ROWS, int BATCH>
 __device__ __forceinline__ void load_operand(uint32_t dst, const CUtensorMap* map, uint32_t bar,
-                                             int mn0, int k0, int bc) {
+                                             int mn0, int k0, int bc, int site, int ext_mn,
+                                             int ext_k) {
+  constexpr int ESZ = 128 / BK;
+  if (MN ? !tma_origin_ok(site, mn0, k0, ext_mn, ext_k, ESZ)
+         : !tma_origin_ok(site, k0, mn0, ext_k, ext_mn, ESZ))
+    return;
   if (MN) {
 #pragma unroll
     for (int j = 0; j < ROWS / 64; ++j) {
@@ -122,6 +130,7 @@ __device__ __forceinline__ void load_operand(uint32_t dst, const CUtensorMap* ma
 __device__ __forceinline__ void store_row16f(const EpiParams& ep, float (&v)[16], int64_t row,
                                              int col0, int N) {
   const int valid = min(16, N - col0);
+  if (!epi_store_ok(ep, SITE_TC_STORE_REG, row, col0, valid)) return;
   epilogue16(ep, v, row, col0, valid);
   const int esz = ep.dtype_c == OJX_F32 ? 4 : 2;
   const int64_t off = (row * ep.ldc + ep.col_offset + col0) * esz;
@@ -222,7 +231,9 @@ __device__ __forceinline__ void epi_chunk_tma_regs(const EpiParams& ep, const St
   }
   fence_proxy_async_smem();  // generic-proxy writes -> visible to the TMA engine
   __syncwarp();
-  if (lane == 0) {
+  // A box whose rows all lie past M (the last M-block of a ragged M) has nothing
+  // to write: the tensor store would clip it whole.
+  if (lane == 0 && row0 < M && tma_origin_ok(SITE_TC_STORE_TMA, col0, row0, N, M, ESZ)) {
 #pragma unroll
     for (int d = 0; d < OJX_MAX_PEERS; ++d) {
       if (d >= ep.n_dst) break;
@@ -336,12 +347,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           const uint32_t sA = sbase + stage * L::STAGE_BYTES;
           const uint32_t sB = sA + L::A_BYTES;
           const int k0 = kb * L::BK;
-          load_operand<A_MN, L::BK, TC_BM, BATCH>(sA, &tmA, fb, m0, k0, abc);
-          load_operand<B_MN, L::BK, BN, BATCH>(sB, &tmB, fb, n0, k0, bbc);
+          load_operand<A_MN, L::BK, TC_BM, BATCH>(sA, &tmA, fb, m0, k0, abc, SITE_TC_LOAD_A, M, K);
+          load_operand<B_MN, L::BK, BN, BATCH>(sB, &tmB, fb, n0, k0, bbc, SITE_TC_LOAD_B, N, K);
           if (KIND == 1) {
-            load_operand<A_MN, L::BK, TC_BM, BATCH>(sB + L::B_BYTES, &tmA2, fb, m0, k0, abc);
+            load_operand<A_MN, L::BK, TC_BM, BATCH>(sB + L::B_BYTES, &tmA2, fb, m0, k0, abc,
+                                                    SITE_TC_LOAD_A, M, K);
             load_operand<B_MN, L::BK, BN, BATCH>(sB + L::B_BYTES + L::A_BYTES, &tmB2, fb, n0, k0,
-                                                 bbc);
+                                                 bbc, SITE_TC_LOAD_B, N, K);
           }
           issued |= 1u << stage;
           issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
@@ -648,6 +660,8 @@ EpiParams make_epi(const ojx_gemm_desc& d, const Dests* dests) {
   ep.unary_packed = 0;
   for (int i = 0; i < d.n_unary && i < OJX_MAX_UNARY; ++i)
     ep.unary_packed |= (static_cast<uint32_t>(d.unary[i]) & 15u) << (4 * i);
+  ep.m_rows = d.M;
+  ep.n_cols = d.N;
   ep.n_dst = 1;
   ep.col_offset = 0;
   for (int i = 0; i < OJX_MAX_PEERS; ++i) ep.dst[i] = d.c;

@@ -4,6 +4,7 @@
 #include <cstdint>
 #include <cstddef>
 #include <atomic>
+#include <nvtx3/nvToolsExt.h>
 #include "../../include/ojx.h"
 
 namespace ojx {
@@ -87,7 +88,21 @@ int launch_attn_softmax(const float* S, int64_t ld, int64_t rows, int M, int nk,
 int launch_sum_columns(void* out, int dt_out, const void* in, int dt_in, int64_t rows, int64_t cols,
                        int64_t ld, cudaStream_t s);
 int read_and_clear_device_error(unsigned int* word);
+// The first failed device-side bounds check (site, coordinate, coordinate, extent)
+// of the OJX_DEBUG_BOUNDS build; debug_bounds_build() says whether this is that build.
+int read_bounds_info(long long info[4]);
+bool debug_bounds_build();
 
 inline int dtype_size(int dt) { return dt == OJX_F32 ? 4 : 2; }
+
+// NVTX range around the enqueue of one GEMM / attention (a profiler such as Nsight
+// Systems or `ncu --nvtx --nvtx-include` sees which library call launched which
+// kernels; with no tool attached the push and pop return at once).
+struct NvtxRange {
+  explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+  NvtxRange(const NvtxRange&) = delete;
+  NvtxRange& operator=(const NvtxRange&) = delete;
+};
 
 }  // namespace ojx

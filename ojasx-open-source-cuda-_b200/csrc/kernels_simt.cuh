@@ -78,7 +78,8 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int64_t col = n0 + tx * 4 + j;
-      if (col < N) store_elem(ep.c, row * ep.ldc + col, ep.dtype_c, epilogue_value(ep, acc[i][j], row, col));
+      if (col < N && epi_store_ok(ep, SITE_SIMT_STORE, row, col, 1))
+        store_elem(ep.c, row * ep.ldc + col, ep.dtype_c, epilogue_value(ep, acc[i][j], row, col));
     }
   }
 }
@@ -349,6 +350,13 @@ int launch_sum_columns(void* out, int dt_out, const void* in, int dt_in, int64_t
   g_launches.fetch_add(1);
   return cuda_status(cudaGetLastError(), "sum_columns launch");
 }
+
+int read_bounds_info(long long info[4]) {
+  return cuda_status(cudaMemcpyFromSymbol(info, g_bounds_info, 4 * sizeof(long long)),
+                     "read bounds record");
+}
+
+bool debug_bounds_build() { return kDebugBounds; }
 
 int read_and_clear_device_error(unsigned int* word) {
   unsigned int zero = 0;

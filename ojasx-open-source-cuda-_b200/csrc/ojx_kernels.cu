@@ -82,6 +82,7 @@ static int noalloc_setup(void** out) {
 
 extern "C" int ojx_gemm_skinny_noalloc(const ojx_gemm_desc* in, ojx_stream stream) {
   using namespace ojx;
+  NvtxRange nvtx("ojx_gemm_skinny_noalloc");
   if (!in) return set_error(OJX_ERR_INVALID, "ojx_gemm_skinny_noalloc: desc is NULL");
   ojx_gemm_desc d = *in;
   if (d.dtype_a != d.dtype_b || (d.dtype_a != OJX_BF16 && d.dtype_a != OJX_F16))

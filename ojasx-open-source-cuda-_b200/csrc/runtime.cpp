@@ -355,12 +355,22 @@ int ojx_poll_device_error(void) {
   unsigned int w = 0;
   int st = read_and_clear_device_error(&w);
   if (st) return st;
+  if (w & 2u) {  // bit 1: a debug-build bounds check failed (sm100.cuh, OJX_DEVERR_BOUNDS)
+    long long info[4] = {0, 0, 0, 0};
+    if ((st = read_bounds_info(info))) return st;
+    return set_error(OJX_ERR_BOUNDS,
+                     "device-side bounds check failed at site %lld (coordinates %lld, %lld; "
+                     "extent %lld); the access was skipped",
+                     info[0], info[1], info[2], info[3]);
+  }
   if (w & 1u)  // bit 0: a bounded wait expired (sm100.cuh, OJX_DEVERR_TIMEOUT)
     return set_error(OJX_ERR_TIMEOUT,
                      "a device-side wait exceeded its budget; the kernel returned early and its "
                      "output is incomplete");
   return OJX_OK;
 }
+
+int ojx_debug_bounds_enabled(void) { return debug_bounds_build() ? 1 : 0; }
 
 int ojx_set_wait_budget(uint64_t cycles) {
   if (cycles == 0) return set_error(OJX_ERR_INVALID, "wait budget must be positive");
@@ -543,10 +553,26 @@ static int gemm_one(const ojx_gemm_desc& d, cudaStream_t s) {
   }
   int st;
   switch (route) {
-    case OJX_ROUTE_SKINNY: st = launch_skinny_gemm(d, s); break;
-    case OJX_ROUTE_TC_F16: st = launch_tc_gemm(d, s); break;
-    case OJX_ROUTE_TC_3XTF32: st = launch_tc_gemm_3xtf32(d, s); break;
-    default: st = launch_simt_gemm(d, s); break;
+    case OJX_ROUTE_SKINNY: {
+      NvtxRange r("ojx_gemm skinny");
+      st = launch_skinny_gemm(d, s);
+      break;
+    }
+    case OJX_ROUTE_TC_F16: {
+      NvtxRange r("ojx_gemm tc_f16");
+      st = launch_tc_gemm(d, s);
+      break;
+    }
+    case OJX_ROUTE_TC_3XTF32: {
+      NvtxRange r("ojx_gemm tc_3xtf32");
+      st = launch_tc_gemm_3xtf32(d, s);
+      break;
+    }
+    default: {
+      NvtxRange r("ojx_gemm simt");
+      st = launch_simt_gemm(d, s);
+      break;
+    }
   }
   if (st == OJX_OK) set_last_route(route);
   return st;
@@ -566,6 +592,7 @@ int ojx_gemm(const ojx_gemm_desc* in, ojx_stream stream) {
 
 int ojx_gemm_batched(const ojx_gemm_desc* in, int64_t batch, int64_t stride_a, int64_t stride_b,
                      int64_t stride_c, int64_t stride_operand, ojx_stream stream) {
+  NvtxRange nvtx("ojx_gemm_batched");
   set_last_route(OJX_ROUTE_NONE);
   if (batch < 0 || stride_a < 0 || stride_b < 0 || stride_c < 0 || stride_operand < 0)
     return set_error(OJX_ERR_INVALID, "ojx_gemm_batched: negative batch or stride");
@@ -664,6 +691,7 @@ extern "C" {
 
 int ojx_gemm_host_io(const ojx_gemm_desc* in, void* dev_a, void* dev_c, int64_t chunk_rows,
                      ojx_stream stream) {
+  NvtxRange nvtx("ojx_gemm_host_io");
   set_last_route(OJX_ROUTE_NONE);
   ojx_gemm_desc d;
   int st = prepare_desc(in, &d, "ojx_gemm_host_io");
@@ -777,6 +805,7 @@ int ojx_attention(void* out, const void* q, const void* k, const void* v, int32_
                   int64_t batch, int64_t heads, int64_t M, int64_t N, int64_t D, float scale,
                   int32_t causal, int64_t max_keys, int32_t flags, ojx_stream stream) {
   set_last_route(OJX_ROUTE_NONE);
+  NvtxRange nvtx("ojx_attention");
   if (batch < 0 || heads < 0 || M < 0 || N < 0 || D < 0)
     return set_error(OJX_ERR_INVALID, "ojx_attention: negative size");
   if (!valid_dtype(dtype)) return set_error(OJX_ERR_INVALID, "ojx_attention: unknown dtype");
@@ -837,6 +866,7 @@ int ojx_attention(void* out, const void* q, const void* k, const void* v, int32_
 
 int ojx_sum_columns(void* out, int32_t dtype_out, const void* in, int32_t dtype_in, int64_t rows,
                     int64_t cols, int64_t ld, ojx_stream s) {
+  NvtxRange nvtx("ojx_sum_columns");
   if (rows < 0 || cols < 0) return set_error(OJX_ERR_INVALID, "ojx_sum_columns: negative size");
   if (cols == 0) return OJX_OK;
   if (!out || (rows > 0 && !in)) return set_error(OJX_ERR_INVALID, "ojx_sum_columns: NULL pointer");
@@ -872,6 +902,7 @@ int ojx_ipc_close_handle(void* dptr) {
 int ojx_gemm_allgather(const ojx_gemm_desc* in, void* const* c_peers, int32_t n_peers,
                        int64_t col_offset, ojx_stream stream) {
   set_last_route(OJX_ROUTE_NONE);
+  NvtxRange nvtx("ojx_gemm_allgather");
   if (!in || !c_peers) return set_error(OJX_ERR_INVALID, "ojx_gemm_allgather: NULL argument");
   if (n_peers < 1 || n_peers > OJX_MAX_PEERS)
     return set_error(OJX_ERR_INVALID, "ojx_gemm_allgather: %d peers (1..%d)", n_peers, OJX_MAX_PEERS);

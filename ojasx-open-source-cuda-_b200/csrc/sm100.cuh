@@ -17,6 +17,51 @@ namespace ojx {
 // unit, ojx_kernels.cu).  Bit 0: a bounded wait expired.
 __device__ unsigned int g_dev_error = 0;
 constexpr unsigned int OJX_DEVERR_TIMEOUT = 1u;
+// Bit 1: a device-side bounds check failed (only the OJX_DEBUG_BOUNDS build checks).
+constexpr unsigned int OJX_DEVERR_BOUNDS = 2u;
+
+// ── debug bounds checks (build with -DOJX_DEBUG_BOUNDS) ─────────────────────
+// Every TMA tile origin and every epilogue store of the GEMM kernels passes through
+// these checks in the debug build (libojx_debug.so); in the normal build they are
+// constant true and vanish.  A failed check sets OJX_DEVERR_BOUNDS, records the
+// first failure in g_bounds_info (site, two coordinates, the extent they broke)
+// and the caller skips the access: nothing traps, a skipped TMA load leaves its
+// consumer to a bounded wait, and the host reads the record through
+// ojx_poll_device_error.
+#ifdef OJX_DEBUG_BOUNDS
+constexpr bool kDebugBounds = true;
+#else
+constexpr bool kDebugBounds = false;
+#endif
+__device__ long long g_bounds_info[4] = {0, 0, 0, 0};
+
+enum BoundsSite : int {
+  SITE_TC_LOAD_A = 1, SITE_TC_LOAD_B = 2, SITE_TC_STORE_TMA = 3, SITE_TC_STORE_REG = 4,
+  SITE_SK_LOAD_W = 5, SITE_SK_LOAD_X = 6, SITE_SK_STORE = 7, SITE_SK_SLOT = 8,
+  SITE_SIMT_STORE = 9, SITE_FA_LOAD = 10, SITE_FA_STORE = 11
+};
+
+__device__ __forceinline__ bool bounds_check(bool ok, int site, long long a, long long b,
+                                             long long ext) {
+  if (!kDebugBounds || ok) return true;
+  if ((atomicOr(&g_dev_error, OJX_DEVERR_BOUNDS) & OJX_DEVERR_BOUNDS) == 0) {
+    g_bounds_info[0] = site;
+    g_bounds_info[1] = a;
+    g_bounds_info[2] = b;
+    g_bounds_info[3] = ext;
+  }
+  return false;
+}
+
+// Origin (c0, c1) of a tiled TMA copy over a tensor with extents (e0, e1) of esz-byte
+// elements: inside the tensor, and c0 * esz on a 16-byte boundary (an unaligned
+// innermost coordinate is an illegal instruction on this GPU).
+__device__ __forceinline__ bool tma_origin_ok(int site, long long c0, long long c1, long long e0,
+                                              long long e1, int esz) {
+  if (!kDebugBounds) return true;
+  const bool ok = c0 >= 0 && c1 >= 0 && c0 < e0 && c1 < e1 && (c0 * esz) % 16 == 0;
+  return bounds_check(ok, site, c0, c1, c0 < e0 ? e1 : e0);
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));

@@ -7,10 +7,16 @@ sm_100 device is present, the first device call raises.
 from __future__ import annotations
 
 import ctypes
+import os
 import pathlib
 import threading
 
-LIB_PATH = pathlib.Path(__file__).resolve().parent / "_lib" / "libojx.so"
+_LIB_DIR = pathlib.Path(__file__).resolve().parent / "_lib"
+# OJX_DEBUG_BOUNDS=1 in the environment (read when the library is first loaded)
+# selects the bounds-checking build: every TMA tile origin and epilogue store is
+# checked on the device and reported through ojx_poll_device_error.
+DEBUG_BOUNDS = os.environ.get("OJX_DEBUG_BOUNDS", "") not in ("", "0")
+LIB_PATH = _LIB_DIR / ("libojx_debug.so" if DEBUG_BOUNDS else "libojx.so")
 
 # status codes (include/ojx.h)
 OJX_OK = 0
@@ -20,6 +26,7 @@ OJX_ERR_CUDA = 3
 OJX_ERR_TIMEOUT = 4
 OJX_ERR_UNSUPPORTED = 5
 OJX_ERR_NOT_INITIALIZED = 6
+OJX_ERR_BOUNDS = 7
 
 F32, BF16, F16 = 0, 1, 2
 UNARY = {"relu": 1, "sigmoid": 2, "tanh": 3, "neg": 4, "abs": 5, "exp": 6, "log": 7,
@@ -90,6 +97,7 @@ _SIGS = {
     "ojx_synchronize": ([], ctypes.c_int),
     "ojx_last_error": ([], ctypes.c_char_p),
     "ojx_poll_device_error": ([], ctypes.c_int),
+    "ojx_debug_bounds_enabled": ([], ctypes.c_int),
     "ojx_set_wait_budget": ([ctypes.c_uint64], ctypes.c_int),
     "ojx_kernel_launch_count": ([], ctypes.c_uint64),
     "ojx_last_route": ([], ctypes.c_int),

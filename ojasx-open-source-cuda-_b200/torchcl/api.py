@@ -105,12 +105,15 @@ def _get_dtype(tensor) -> torch.dtype:
 
 
 def _get_buf(tensor) -> CLBuffer:
-    """The device buffer of a handle, materialising a lazy node first."""
+    """The device buffer of a handle, materialising a lazy node (or finishing a
+    deferred upload) first."""
     e = _elem(tensor)
     tid = getattr(e, "_torchcl_id", None)
     if tid is not None:
         with _buffer_lock:
             buf = _opencl_buffers.get(tid)
+        if buf is None and getattr(e, "_torchcl_host", None) is not None:
+            buf = _finish_upload(e)
         if buf is None and _is_lazy(e):
             materialize_lazy_tensor(e)
             buf = _opencl_buffers[tid]
@@ -136,7 +139,8 @@ def is_opencl_tensor(tensor: Any) -> bool:
     if tid is None:
         return False
     with _buffer_lock:
-        return tid in _opencl_buffers or _is_lazy(e)
+        return (tid in _opencl_buffers or _is_lazy(e)
+                or getattr(e, "_torchcl_host", None) is not None)
 
 
 # ── lazy nodes ───────────────────────────────────────────────────────────
@@ -316,21 +320,134 @@ def materialize_lazy_tensor(tensor) -> None:
 
 # ── data movement ───────────────────────────────────────────────────────
 
+# A pinned host tensor of at least this many bytes is uploaded when its data is
+# first needed (see to_opencl) rather than at once.
+DEFERRED_UPLOAD_MIN_BYTES = 1 << 20
+
+
 def to_opencl(tensor: torch.Tensor):
-    """Copy a CPU tensor (float32 / bfloat16 / float16) to the device."""
+    """Copy a CPU tensor (float32 / bfloat16 / float16) to the device.
+
+    A pageable tensor is copied at once, as the reference does (api.py:210-217).
+    A contiguous pinned tensor (torch's pin_memory) of 1 MiB or more is instead read
+    when its device data is first needed, which lets to_cpu() of a GEMM on it
+    overlap the upload, the GEMM and the download chunk by chunk.  Such a tensor
+    follows torch's non_blocking contract: leave it unmodified until the handle
+    has been used (or torchcl.synchronize() has returned)."""
     if is_opencl_tensor(tensor):
         return tensor
+    t = tensor.detach()
+    if (t.device.type == "cpu" and t.is_contiguous() and _pinned(t)
+            and t.numel() * t.element_size() >= DEFERRED_UPLOAD_MIN_BYTES
+            and t.dtype in (torch.float32, torch.bfloat16, torch.float16)):
+        handle, _ = _make_handle(tuple(t.shape), t.dtype)
+        handle._torchcl_host = t
+        return _wrap(handle)
     cl_buf = get_engine().tensor_to_buffer(tensor)
     return _wrap_output(cl_buf, tuple(tensor.shape), tensor.dtype)
 
 
+def _pinned(t: torch.Tensor) -> bool:
+    try:
+        return bool(t.is_pinned())
+    except RuntimeError:  # torch without a usable CUDA runtime: nothing is pinned
+        return False
+
+
+def _finish_upload(e) -> CLBuffer:
+    """Upload a deferred handle's host tensor now (blocking) and register the buffer."""
+    with _buffer_lock:
+        buf = _opencl_buffers.get(e._torchcl_id)
+        host = getattr(e, "_torchcl_host", None)
+        if buf is not None or host is None:
+            return buf
+        buf = get_engine().tensor_to_buffer(host)
+        _attach(e, buf)
+        return buf
+
+
+def _attach(e, cl_buf: CLBuffer) -> None:
+    """Make cl_buf the device buffer of handle e (which had none)."""
+    with _buffer_lock:
+        _opencl_buffers[e._torchcl_id] = cl_buf
+        if getattr(e, "_torchcl_host", None) is not None:
+            e._torchcl_host = None
+    weakref.finalize(e, _cleanup_buffer, cl_buf)
+
+
+def _host_io_plan(e):
+    """(A handle, B handle) when e is a lazy GEMM that to_cpu can run with A read
+    from the host: A a deferred (pinned) upload used untransposed, B on the device
+    or uploadable, no forced-half route, 16-bit or fp32 output.  Else None."""
+    if _lazy_type(e) != "gemm" or len(_get_shape(e)) != 2:
+        return None
+    with _buffer_lock:
+        if e._torchcl_id in _opencl_buffers:
+            return None
+    g = e._lazy_gemm
+    if g.get("precision") == "half" and _get_dtype(e) == torch.float32:
+        return None  # the forced fp16 route of fp32 inputs (casts around a half GEMM)
+    a_src, ta = _gemm_source(e._lazy_inputs[0])
+    if ta or getattr(a_src, "_torchcl_host", None) is None:
+        return None
+    return a_src, e._lazy_inputs[1]
+
+
+def _to_cpu_host_io(e, a_src) -> torch.Tensor:
+    """to_cpu of a lazy GEMM whose A waits in pinned host memory: one
+    ojx_gemm_host_io call uploads A in row chunks, runs each chunk's fused GEMM and
+    downloads each finished chunk into a pinned output while the next one uploads.
+    A's handle keeps the uploaded copy and the node keeps its device result, as if
+    both had been materialised."""
+    engine = get_engine()
+    pool = get_buffer_pool()
+    g = e._lazy_gemm
+    b_src, tb = _gemm_source(e._lazy_inputs[1])
+    b_buf = _get_buf(b_src)
+    operand = g.get("operand")
+    op_buf = _get_buf(operand) if operand is not None else None
+    M, N = _get_shape(e)
+    K = g["K"]
+    dtype = _get_dtype(e)
+    host_a = a_src._torchcl_host
+    try:
+        out = torch.empty((M, N), dtype=dtype, pin_memory=True)
+    except RuntimeError:
+        out = torch.empty((M, N), dtype=dtype)
+    dev_a = pool.allocate(host_a.numel() * host_a.element_size(), host_a.dtype, tuple(host_a.shape))
+    dev_c = engine.allocate_output((M, N), dtype)
+    try:
+        engine.gemm_host_io(host_a.data_ptr(), b_buf, out.data_ptr(), dev_a, dev_c, M, N, K,
+                            dtype_a=host_a.dtype, dtype_b=_get_dtype(b_src), dtype_c=dtype,
+                            trans_b=tb, operand=op_buf, operand_kind=g.get("operand_kind"),
+                            operand_dtype=_get_dtype(operand) if operand is not None else None,
+                            binary=g.get("binary", "add"),
+                            operand_is_lhs=g.get("operand_is_lhs", False), unary=e._lazy_ops,
+                            fp32_mode=g.get("fp32_mode", L.FP32_AUTO))
+        _sync()
+    except Exception:
+        pool.free(dev_a)
+        pool.free(dev_c)
+        raise
+    _attach(a_src, dev_a)
+    _attach(e, dev_c)
+    return out
+
+
 def to_cpu(tensor):
-    """Copy a device tensor back to a CPU torch tensor (materialising it first)."""
+    """Copy a device tensor back to a CPU torch tensor (materialising it first).
+
+    For a lazy GEMM whose A is a deferred pinned upload (to_opencl of a pinned
+    tensor), the upload, the fused GEMM and the download run as one overlapped
+    pipeline, and the result is returned in pinned memory."""
     if tensor is None:
         return None
     e = _elem(tensor)
     if not is_opencl_tensor(e):
         return tensor
+    plan = _host_io_plan(e)
+    if plan is not None:
+        return _to_cpu_host_io(e, plan[0])
     return get_engine().buffer_to_tensor(_get_buf(e), _get_shape(e), _get_dtype(e))
 
 

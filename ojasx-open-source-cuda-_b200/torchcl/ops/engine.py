@@ -94,6 +94,39 @@ class OpenCLEngine:
              batch=None, stride_a=0, stride_b=0, stride_c=0, stride_operand=0) -> str:
         """One fused GEMM: out = unary(...(bin(op(A) @ op(B), operand))).  With `batch`,
         `batch` problems whose operands are stride_* elements apart (ojx_gemm_batched)."""
+        d = self._desc(a_buf, b_buf, out_buf, M, N, K, dtype_a=dtype_a, dtype_b=dtype_b,
+                       dtype_c=dtype_c, trans_a=trans_a, trans_b=trans_b, lda=lda, ldb=ldb,
+                       ldc=ldc, operand=operand, operand_kind=operand_kind,
+                       operand_dtype=operand_dtype, ld_operand=ld_operand, binary=binary,
+                       operand_is_lhs=operand_is_lhs, unary=unary, fp32_mode=fp32_mode,
+                       flags=flags)
+        q = get_queue() if stream is None else stream
+        lib = L.lib()
+        if batch is None:
+            L.check(lib.ojx_gemm(ctypes.byref(d), q), "gemm")
+        else:
+            L.check(lib.ojx_gemm_batched(ctypes.byref(d), int(batch), int(stride_a), int(stride_b),
+                                         int(stride_c), int(stride_operand), q), "gemm_batched")
+        self.last_route = L.ROUTES.get(lib.ojx_last_route(), "?")
+        return self.last_route
+
+    def gemm_host_io(self, host_a: int, b_buf, host_c: int, dev_a, dev_c, M: int, N: int, K: int,
+                     **kw) -> str:
+        """The same fused GEMM with A and C in (pinned) host memory: ojx_gemm_host_io
+        uploads A in row chunks into dev_a, runs each chunk's GEMM into dev_c and
+        downloads it to host_c while the next chunk uploads, all ordered after the
+        work already queued on the current stream.  Returns the route."""
+        d = self._desc(host_a, b_buf, host_c, M, N, K, **kw)
+        lib = L.lib()
+        L.check(lib.ojx_gemm_host_io(ctypes.byref(d), _addr(dev_a), _addr(dev_c), 0, get_queue()),
+                "gemm_host_io")
+        self.last_route = L.ROUTES.get(lib.ojx_last_route(), "?")
+        return self.last_route
+
+    def _desc(self, a_buf, b_buf, out_buf, M: int, N: int, K: int, *, dtype_a=None, dtype_b=None,
+              dtype_c=None, trans_a=False, trans_b=False, lda=0, ldb=0, ldc=0, operand=None,
+              operand_kind=None, operand_dtype=None, ld_operand=0, binary="add",
+              operand_is_lhs=False, unary=(), fp32_mode=L.FP32_AUTO, flags=0) -> L.GemmDesc:
         d = L.GemmDesc()
         d.M, d.N, d.K = int(M), int(N), int(K)
         d.dtype_a = ojx_dtype(dtype_a if dtype_a is not None else getattr(a_buf, "dtype", None))
@@ -120,15 +153,7 @@ class OpenCLEngine:
             d.unary[i] = c
         d.fp32_mode = int(fp32_mode)
         d.flags = int(flags)
-        q = get_queue() if stream is None else stream
-        lib = L.lib()
-        if batch is None:
-            L.check(lib.ojx_gemm(ctypes.byref(d), q), "gemm")
-        else:
-            L.check(lib.ojx_gemm_batched(ctypes.byref(d), int(batch), int(stride_a), int(stride_b),
-                                         int(stride_c), int(stride_operand), q), "gemm_batched")
-        self.last_route = L.ROUTES.get(lib.ojx_last_route(), "?")
-        return self.last_route
+        return d
 
     def run_matmul(self, a_buf, b_buf, out_buf, M, N, K, use_tiled: bool = True) -> None:
         """C[M,N] = A[M,K] @ B[K,N] (engine.py:156-185)."""
