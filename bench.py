@@ -327,6 +327,8 @@ def run_ours(args, cfg, world, rank, local):
     d.operand_kind, d.binary_op = L.OPERAND_ROW, L.BINARY["add"]
     d.n_unary, d.unary[0] = 1, L.UNARY[cfg["act"]]
     d.fp32_mode = L.FP32_3XTF32 if code == L.F32 and M > 16 else L.FP32_AUTO
+    if args.pair:
+        d.flags |= L.FLAG_PAIR
 
     step_no = [0]
 
@@ -934,6 +936,8 @@ def main() -> int:
                     help="one GPU: time this many problems of the config's shape in one batched GEMM")
     ap.add_argument("--train", action="store_true",
                     help="one GPU: time a linear-layer training step (forward + backward GEMMs)")
+    ap.add_argument("--pair", action="store_true",
+                    help="CTA-pair (cta_group::2) tcgen05 tiles where they apply (one-CTA tiles otherwise)")
     ap.add_argument("--graph", action="store_true",
                     help="one GPU: also time public-API dispatch vs graph replay of one step")
     args = ap.parse_args()

@@ -114,6 +114,8 @@ typedef struct ojx_gemm_desc {
 #define OJX_GEMM_FLAG_FORCE_SIMT 0x1   /* SIMT kernel for any dtype */
 #define OJX_GEMM_FLAG_NO_SKINNY 0x2    /* never take the split-K skinny route */
 #define OJX_GEMM_FLAG_FORCE_SKINNY 0x4 /* skinny route when M <= 16 even if a tile kernel would fit */
+#define OJX_GEMM_FLAG_PAIR 0x8         /* CTA-pair tiles (cta_group::2, 256 x 256) where they apply:
+                                          ~2 % faster in short runs, slower under the power cap */
 
 /* Which kernel family ojx_gemm used for its most recent call on this thread. */
 enum {

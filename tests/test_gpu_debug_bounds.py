@@ -42,6 +42,7 @@ cases = [  # (M, N, K, dtype, trans_a, trans_b, route)
     (16, 264, 4160, torch.float16, False, False, "skinny"),
     (33, 65, 31, torch.float32, False, False, "tc_3xtf32"),
     (129, 127, 33, torch.float32, True, True, "tc_3xtf32"),
+    (2100, 2504, 520, torch.bfloat16, False, True, "tc_f16"),  # CTA pairs (flag 0x8), ragged
     (31, 7, 65, torch.bfloat16, False, False, "simt"),
     (7, 33, 1, torch.float32, False, False, "simt"),
 ]
@@ -50,7 +51,7 @@ for M, N, K, dt, ta, tb, want in cases:
     B = randn(K + 1, (N, K) if tb else (K, N), dt, scale=0.1)
     bias = randn(N, (N,), dt, scale=0.1)
     C, route = run_gemm(A, B, trans_a=ta, trans_b=tb, operand=bias, kind="row", unary=("gelu",),
-                        fp32_mode=1 if want == "tc_3xtf32" else 0)
+                        fp32_mode=1 if want == "tc_3xtf32" else 0, flags=0x8 if M > 2000 else 0)
     assert route == want, (M, N, K, route, want)
     L.check(lib.ojx_poll_device_error(), f"{(M, N, K)} {route}")
     ref = oracle_gemm(A, B, trans_a=ta, trans_b=tb, operand=bias, kind="row", unary=("gelu",))
