@@ -37,7 +37,10 @@
 // kernel's writes.
 #include <cuda_runtime.h>
 #include <algorithm>
+#include <cstdlib>
+#include <map>
 #include <mutex>
+#include <tuple>
 #include <unordered_map>
 #include "sm100.cuh"
 #include "epilogue.cuh"
@@ -583,6 +586,7 @@ bool skinny_supported(const ojx_gemm_desc& d) {
 
 static std::atomic<unsigned int> g_skinny_epoch{1};
 
+
 // Host-side partition bookkeeping; mirrors unit_begin / cta_of_unit.
 static int skinny_max_contrib(int n_groups, int KB, long long U, int G) {
   auto ub = [&](long long c) { return c * U / G; };
@@ -599,6 +603,36 @@ static int skinny_max_contrib(int n_groups, int KB, long long U, int G) {
     mx = std::max<int>(mx, static_cast<int>(b - a + 1));
   }
   return mx;
+}
+
+// CTAs of a skinny launch.  The group whose split-K contributors finish last sets the
+// tail: its last arriver waits for, and reads, every other contributor's partial
+// slot.  Among grids within 8 % of the SM count, take the largest one whose busiest
+// group has the fewest contributors.  Measured at cfg4's shape (56 groups of 64
+// k-blocks): 140 CTAs give every group 3 contributors and 23.8 / 24.1 / 27.5 us per
+// launch at M = 1 / 4 / 16, while every grid of 132-148 CTAs with 4-contributor
+// groups took 24.7-25.8 / 25.2-25.8 / 28.6-29.9 us; 112 CTAs (2 per group) lost the
+// gain again in streaming bandwidth.  Cached per (groups, k blocks, SMs).
+static int skinny_grid(int n_groups, int KB, long long U, int sm_count) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, int>, int>* cache = new std::map<std::tuple<int, int, int>, int>();
+  const long long gmax = std::min<long long>(U, sm_count);
+  if (gmax <= 1) return static_cast<int>(std::max<long long>(gmax, 1));
+  const auto key = std::make_tuple(n_groups, KB, sm_count);
+  std::lock_guard<std::mutex> g(mu);
+  auto it = cache->find(key);
+  if (it != cache->end()) return it->second;
+  const int gmin = static_cast<int>(std::max<long long>(1, (gmax * 92 + 99) / 100));
+  int best = static_cast<int>(gmax), best_c = skinny_max_contrib(n_groups, KB, U, best);
+  for (int G = best - 1; G >= gmin; --G) {
+    const int c = skinny_max_contrib(n_groups, KB, U, G);
+    if (c < best_c) {
+      best = G;
+      best_c = c;
+    }
+  }
+  (*cache)[key] = best;
+  return best;
 }
 
 // Byte ranges written by the last eager skinny launch on each stream.  The next
@@ -623,7 +657,7 @@ int launch_skinny_gemm(const ojx_gemm_desc& d, cudaStream_t s, const Dests* dest
   p.KB = (p.K + SK_BK - 1) / SK_BK;
   p.U = static_cast<long long>(p.n_groups) * p.KB;
   const DeviceProps& dp = current_props();
-  p.G = static_cast<int>(std::min<long long>(p.U, dp.sm_count));
+  p.G = skinny_grid(p.n_groups, p.KB, p.U, dp.sm_count);
   p.maxc = skinny_max_contrib(p.n_groups, p.KB, p.U, p.G);
   const size_t part_bytes = static_cast<size_t>(p.n_groups) * p.maxc * SK_SLOT * 4;
   p.partials = static_cast<float*>(stream_workspace(s, part_bytes, 1, false));

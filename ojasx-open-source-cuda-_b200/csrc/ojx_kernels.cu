@@ -123,7 +123,7 @@ extern "C" int ojx_gemm_skinny_noalloc(const ojx_gemm_desc* in, ojx_stream strea
   p.n_groups = (p.N + SK_TPU * SK_BN - 1) / (SK_TPU * SK_BN);
   p.KB = (p.K + SK_BK - 1) / SK_BK;
   p.U = static_cast<long long>(p.n_groups) * p.KB;
-  p.G = static_cast<int>(std::min<long long>(p.U, dp.sm_count));
+  p.G = skinny_grid(p.n_groups, p.KB, p.U, dp.sm_count);  // the same grid as ojx_gemm's skinny route
   p.maxc = skinny_max_contrib(p.n_groups, p.KB, p.U, p.G);
   const size_t counter_bytes = static_cast<size_t>(p.n_groups) * 8;
   const size_t part_bytes = static_cast<size_t>(p.n_groups) * p.maxc * SK_SLOT * 4;
