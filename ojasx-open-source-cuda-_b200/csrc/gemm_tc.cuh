@@ -71,7 +71,9 @@ struct TcLayout {
   static constexpr int B_BYTES = B_ROWS * 128;
   static constexpr int NPART = KIND == 0 ? 1 : 2;  // tf32: hi and lo copies
   static constexpr int STAGE_BYTES = (A_BYTES + B_BYTES) * NPART;
-  static constexpr uint32_t TMEM_COLS = 2 * BN;
+  // 3xTF32 keeps two accumulators per tile (the Ah*Bh term and the two small terms),
+  // so each of the two TMEM buffers is 2*BN columns wide.
+  static constexpr uint32_t TMEM_COLS = (KIND == 1 ? 4 : 2) * BN;
   static constexpr int BAR_BYTES = 256;
   // TMA-store epilogue: one 32-row x 128-byte (swizzled) staging box per epilogue warp.
   static constexpr int STAGE_OUT_BYTES = 32 * 128;
@@ -380,8 +382,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           // the leader alone announces the pair's total.
           const uint32_t fb = CG == 2 ? mapa_shared(full_bar(stage), 0) : full_bar(stage);
           if (leader) mbar_arrive_expect_tx(full_bar(stage), CG * L::STAGE_BYTES);
+          // stage layout: KIND 0 [A][B]; KIND 1 [A_hi][A_lo][B_hi][B_lo] (B_hi and B_lo
+          // adjacent: one N = 2*BN MMA reads both)
           const uint32_t sA = sbase + stage * L::STAGE_BYTES;
-          const uint32_t sB = sA + L::A_BYTES;
+          const uint32_t sB = sA + L::NPART * L::A_BYTES;
           const int k0 = kb * L::BK;
           // (the second CTA's half of a ragged pair tile may start past M or N and read
           // the zero fill: the debug checks take the pair tile's extent for a pair)
@@ -390,10 +394,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           load_operand<B_MN, L::BK, L::B_ROWS, BATCH, CG>(sB, &tmB, fb, n0, k0, bbc, SITE_TC_LOAD_B,
                                                          CG == 2 ? tiles_n * BN : N, K);
           if (KIND == 1) {
-            load_operand<A_MN, L::BK, TC_BM, BATCH>(sB + L::B_BYTES, &tmA2, fb, m0, k0, abc,
+            load_operand<A_MN, L::BK, TC_BM, BATCH>(sA + L::A_BYTES, &tmA2, fb, m0, k0, abc,
                                                     SITE_TC_LOAD_A, M, K);
-            load_operand<B_MN, L::BK, BN, BATCH>(sB + L::B_BYTES + L::A_BYTES, &tmB2, fb, n0, k0,
-                                                 bbc, SITE_TC_LOAD_B, N, K);
+            load_operand<B_MN, L::BK, BN, BATCH>(sB + L::B_BYTES, &tmB2, fb, n0, k0, bbc,
+                                                 SITE_TC_LOAD_B, N, K);
           }
           issued |= 1u << stage;
           issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
@@ -418,6 +422,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     // ── MMA issuer (one thread; CG = 2: the leader's, for the pair) ──────────
     if (lane == 0 && leader) {
       constexpr uint32_t IDESC = make_idesc(FMT, A_MN, B_MN, TC_BM * CG, BN);
+      // 3xTF32: Ah * [Bh | Bl] as one N = 2*BN MMA (the two products land side by side:
+      // columns [0, BN) hold Ah*Bh, [BN, 2*BN) Ah*Bl), then Al * Bh added to the second
+      // half.  The large term and the two small ones are accumulated apart and added in
+      // the epilogue.
+      constexpr uint32_t IDESC_WIDE = make_idesc(FMT, A_MN, B_MN, TC_BM, 2 * BN);
+      constexpr uint32_t ACC_COLS = (KIND == 1 ? 2 : 1) * BN;  // TMEM columns per buffer
       int stage = 0, acc = 0;
       uint32_t phase = 0, acc_phase = 0;
       bool ok = true;
@@ -431,7 +441,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
+          const uint32_t d = tmem_base + static_cast<uint32_t>(acc * ACC_COLS);
           const int kend = min(KB, kc + KCH);
           for (int kb = kc; kb < kend; ++kb) {
             if (!mbar_wait(full_bar(stage), phase, budget, s_abort)) {
@@ -440,7 +450,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             }
             tc_fence_after();
             const uint32_t sA = sbase + stage * L::STAGE_BYTES;
-            const uint32_t sB = sA + L::A_BYTES;
+            const uint32_t sB = sA + L::NPART * L::A_BYTES;
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks) {
               const uint64_t ad = operand_desc<A_MN, L::BK>(sA, ks);
@@ -451,11 +461,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
               } else if (KIND == 0) {
                 mma_f16(d, ad, bd, IDESC, accum);
               } else {
-                const uint64_t ad_lo = operand_desc<A_MN, L::BK>(sB + L::B_BYTES, ks);
-                const uint64_t bd_lo = operand_desc<B_MN, L::BK>(sB + L::B_BYTES + L::A_BYTES, ks);
-                mma_tf32(d, ad_lo, bd, IDESC, accum);  // Al * Bh
-                mma_tf32(d, ad, bd_lo, IDESC, 1u);     // Ah * Bl
-                mma_tf32(d, ad, bd, IDESC, 1u);        // Ah * Bh
+                const uint64_t ad_lo = operand_desc<A_MN, L::BK>(sA + L::A_BYTES, ks);
+                mma_tf32(d, ad, bd, IDESC_WIDE, accum);  // [Ah*Bh | Ah*Bl]
+                mma_tf32(d + BN, ad_lo, bd, IDESC, 1u);  // Ah*Bl + Al*Bh
               }
             }
             // smem slot free (in both CTAs of a pair) once these MMAs have read it
@@ -504,16 +512,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       for (int kc = 0; kc < KB; kc += KCH) {
         if (!mbar_wait(tfull_bar(acc), acc_phase, budget, s_abort)) return false;
         tc_fence_after();
+        // buffer acc: columns [0, BN) the Ah*Bh sums, [BN, 2*BN) the small terms
         const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
-                            static_cast<uint32_t>(acc * BN + half * HC);
+                            static_cast<uint32_t>(acc * 2 * BN + half * HC);
 #pragma unroll
         for (int i = 0; i < HC; i += 16) {
-          uint32_t r[16];
+          uint32_t r[16], t[16];
           tmem_ld16(tb + i, r);
+          tmem_ld16(tb + BN + i, t);
           tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 16; ++j)
-            sum[i + j] = kc == 0 ? __uint_as_float(r[j]) : sum[i + j] + __uint_as_float(r[j]);
+          for (int j = 0; j < 16; ++j) {
+            const float run = __uint_as_float(r[j]) + __uint_as_float(t[j]);
+            sum[i + j] = kc == 0 ? run : sum[i + j] + run;
+          }
         }
         tc_fence_before();
         __syncwarp();
