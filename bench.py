@@ -329,6 +329,8 @@ def run_ours(args, cfg, world, rank, local):
     d.fp32_mode = L.FP32_3XTF32 if code == L.F32 and M > 16 else L.FP32_AUTO
     if args.pair:
         d.flags |= L.FLAG_PAIR
+    if args.skinny_counter:
+        d.flags |= L.FLAG_SKINNY_COUNTER
 
     step_no = [0]
 
@@ -938,6 +940,9 @@ def main() -> int:
                     help="one GPU: time a linear-layer training step (forward + backward GEMMs)")
     ap.add_argument("--pair", action="store_true",
                     help="CTA-pair (cta_group::2) tcgen05 tiles where they apply (one-CTA tiles otherwise)")
+    ap.add_argument("--skinny-counter", action="store_true",
+                    help="skinny route: hand split-K partials over through the arrival counter "
+                         "(the tagged hand-off otherwise, where it applies)")
     ap.add_argument("--graph", action="store_true",
                     help="one GPU: also time public-API dispatch vs graph replay of one step")
     args = ap.parse_args()

@@ -116,6 +116,9 @@ typedef struct ojx_gemm_desc {
 #define OJX_GEMM_FLAG_FORCE_SKINNY 0x4 /* skinny route when M <= 16 even if a tile kernel would fit */
 #define OJX_GEMM_FLAG_PAIR 0x8         /* CTA-pair tiles (cta_group::2, 256 x 256) where they apply:
                                           ~2 % faster in short runs, slower under the power cap */
+#define OJX_GEMM_FLAG_SKINNY_COUNTER 0x10 /* skinny route: hand split-K partials over through the
+                                             arrival counter even where the tagged hand-off applies
+                                             (same sums, same result bits) */
 
 /* Which kernel family ojx_gemm used for its most recent call on this thread. */
 enum {

@@ -85,6 +85,13 @@ struct SkinnyParams {
   int silence_producer;
   int trigger_early;  // let the next launch in after the last W load is issued
   int early_w;        // W of the first SK_STAGES units may be loaded before the dependency wait
+  // Tagged hand-off (see the epilogue): each split group is finished by its last
+  // contributor, which reads the others' partials from `tagged_parts` (one 64-bit
+  // word per value: epoch << 32 | fp32 bits) as soon as they carry this launch's
+  // epoch.  Only used when every CTA covers at most KB units, so that a group's
+  // last contributor reaches that group at the very end of its own stream.
+  int tagged;
+  unsigned long long* tagged_parts;
 };
 
 __device__ __forceinline__ long long unit_begin(int c, const SkinnyParams& p) {
@@ -359,6 +366,8 @@ __global__ void __launch_bounds__(SK_THREADS, 2)
           ncontrib = c_last - c_first + 1;
         }
         const int jc = blockIdx.x - c_first;
+        // Tagged hand-off: the group's last contributor (highest CTA index) finishes it.
+        const bool tag_finisher = p.tagged && !whole && jc == ncontrib - 1;
         // With more than 4 rows, the last finish of the CTA (its ring is idle by
         // then: every MMA has completed) bulk-copies the other contributors' slots
         // into the ring, one round trip instead of one per 4 rows; with up to 4
@@ -386,7 +395,100 @@ __global__ void __launch_bounds__(SK_THREADS, 2)
         for (int j = 0; j < SK_TPU; ++j)
 #pragma unroll
           for (int m = 0; m < SK_MN; ++m) v[j][m] = __uint_as_float(r[j][m]);
-        if (!whole) {
+        if (!whole && p.tagged && !tag_finisher) {
+          // Tagged hand-off, contributor side: publish each value beside this
+          // launch's epoch in one 64-bit word and move on (no barrier, fence or
+          // counter: every word validates itself, and this CTA finishes nothing).
+          unsigned long long* slot = p.tagged_parts +
+                                     (static_cast<long long>(g) * p.maxc + jc) * SK_SLOT + q * 32 + lane;
+          const unsigned long long tag = static_cast<unsigned long long>(p.epoch) << 32;
+#pragma unroll
+          for (int j = 0; j < SK_TPU; ++j)
+#pragma unroll
+            for (int m = 0; m < SK_MN; ++m)
+              if (m < p.M) st_relaxed_gpu_u64(slot + (j * SK_MN + m) * SK_BN, tag | __float_as_uint(v[j][m]));
+          finish = false;
+        } else if (tag_finisher) {
+          // Tagged hand-off, finisher side: this CTA reached the group at the end of
+          // its stream; the other contributors (lower CTA indices, none of which
+          // waits on anything) publish their words at about the same time or
+          // earlier.  Poll them until every word carries this launch's epoch
+          // (bounded), and sum in contributor order with this CTA's own partial
+          // last, which is its place in that order: the same sums as the counter
+          // hand-off below.
+          const unsigned long long* tb =
+              p.tagged_parts + static_cast<long long>(g) * p.maxc * SK_SLOT + q * 32 + lane;
+          const unsigned int want = p.epoch;
+          const unsigned long long valid = static_cast<unsigned long long>(want) << 32;
+          const long long t0 = clock64();
+          bool ok = true;
+#pragma unroll
+          for (int mc = 0; mc < SK_MN / 4; ++mc) {
+            if (4 * mc >= p.M || !ok) break;
+            float sum[SK_TPU][4];
+#pragma unroll
+            for (int j = 0; j < SK_TPU; ++j)
+#pragma unroll
+              for (int mm = 0; mm < 4; ++mm) sum[j][mm] = 0.0f;
+            for (int jj0 = 0; jj0 < jc && ok; jj0 += 2) {
+              unsigned long long t[2][SK_TPU][4];
+#pragma unroll
+              for (int bb = 0; bb < 2; ++bb)
+#pragma unroll
+                for (int j = 0; j < SK_TPU; ++j)
+#pragma unroll
+                  for (int mm = 0; mm < 4; ++mm)
+                    t[bb][j][mm] = (jj0 + bb < jc && 4 * mc + mm < p.M)
+                                       ? ld_relaxed_gpu_u64(tb + static_cast<long long>(jj0 + bb) * SK_SLOT +
+                                                            (j * SK_MN + 4 * mc + mm) * SK_BN)
+                                       : valid;
+              while (true) {
+                bool all = true;
+#pragma unroll
+                for (int bb = 0; bb < 2; ++bb)
+#pragma unroll
+                  for (int j = 0; j < SK_TPU; ++j)
+#pragma unroll
+                    for (int mm = 0; mm < 4; ++mm) all &= static_cast<unsigned int>(t[bb][j][mm] >> 32) == want;
+                if (all) break;
+                if (*s_abort) {
+                  ok = false;
+                  break;
+                }
+                if (static_cast<uint64_t>(clock64() - t0) > p.budget) {
+                  *s_abort = 1;
+                  atomicOr(&g_dev_error, OJX_DEVERR_TIMEOUT);
+                  ok = false;
+                  break;
+                }
+#pragma unroll
+                for (int bb = 0; bb < 2; ++bb)
+#pragma unroll
+                  for (int j = 0; j < SK_TPU; ++j)
+#pragma unroll
+                    for (int mm = 0; mm < 4; ++mm)
+                      if (static_cast<unsigned int>(t[bb][j][mm] >> 32) != want)
+                        t[bb][j][mm] = ld_relaxed_gpu_u64(tb + static_cast<long long>(jj0 + bb) * SK_SLOT +
+                                                          (j * SK_MN + 4 * mc + mm) * SK_BN);
+              }
+#pragma unroll
+              for (int bb = 0; bb < 2; ++bb)
+                if (jj0 + bb < jc)
+#pragma unroll
+                  for (int j = 0; j < SK_TPU; ++j)
+#pragma unroll
+                    for (int mm = 0; mm < 4; ++mm)
+                      sum[j][mm] += __uint_as_float(static_cast<unsigned int>(t[bb][j][mm]));
+            }
+#pragma unroll
+            for (int j = 0; j < SK_TPU; ++j)
+#pragma unroll
+              for (int mm = 0; mm < 4; ++mm) v[j][4 * mc + mm] = sum[j][mm] + v[j][4 * mc + mm];
+          }
+          // The four epilogue warps meet at named barriers below: any thread that
+          // gave up stops all four.
+          if (named_bar_red_or(1, 128, !ok)) break;
+        } else if (!whole) {
           float* slot = p.partials + (static_cast<long long>(g) * p.maxc + jc) * SK_SLOT +
                         q * 32 + lane;
 #pragma unroll
@@ -659,12 +761,26 @@ int launch_skinny_gemm(const ojx_gemm_desc& d, cudaStream_t s, const Dests* dest
   const DeviceProps& dp = current_props();
   p.G = skinny_grid(p.n_groups, p.KB, p.U, dp.sm_count);
   p.maxc = skinny_max_contrib(p.n_groups, p.KB, p.U, p.G);
-  const size_t part_bytes = static_cast<size_t>(p.n_groups) * p.maxc * SK_SLOT * 4;
-  p.partials = static_cast<float*>(stream_workspace(s, part_bytes, 1, false));
-  if (!p.partials) return workspace_error();
-  p.counters = static_cast<unsigned long long*>(
-      stream_workspace(s, static_cast<size_t>(p.n_groups) * 8, 2, /*zero=*/true));
-  if (!p.counters) return workspace_error();
+  // Capture status first: the tagged hand-off needs a fresh epoch per execution,
+  // which a replayed graph (fixed kernel parameters) does not give.
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (s && cudaStreamIsCapturing(s, &cs) != cudaSuccess) cs = cudaStreamCaptureStatusActive;
+  const bool eager = cs == cudaStreamCaptureStatusNone;
+  p.tagged = eager && !(d.flags & OJX_GEMM_FLAG_SKINNY_COUNTER) && (p.U + p.G - 1) / p.G <= p.KB ? 1 : 0;
+  if (p.tagged) {
+    // Its own zero-initialised slot: the words there only ever carry the epochs of
+    // earlier skinny launches (or 0), never this launch's.
+    p.tagged_parts = static_cast<unsigned long long*>(
+        stream_workspace(s, static_cast<size_t>(p.n_groups) * p.maxc * SK_SLOT * 8, 6, /*zero=*/true));
+    if (!p.tagged_parts) return workspace_error();
+  } else {
+    const size_t part_bytes = static_cast<size_t>(p.n_groups) * p.maxc * SK_SLOT * 4;
+    p.partials = static_cast<float*>(stream_workspace(s, part_bytes, 1, false));
+    if (!p.partials) return workspace_error();
+    p.counters = static_cast<unsigned long long*>(
+        stream_workspace(s, static_cast<size_t>(p.n_groups) * 8, 2, /*zero=*/true));
+    if (!p.counters) return workspace_error();
+  }
   p.epoch = g_skinny_epoch.fetch_add(1);
   if (p.epoch == 0) p.epoch = g_skinny_epoch.fetch_add(1);
   p.budget = g_wait_budget.load();
@@ -687,9 +803,6 @@ int launch_skinny_gemm(const ojx_gemm_desc& d, cudaStream_t s, const Dests* dest
   // plain stream order and never let the next kernel in early): the grid may
   // start while the previous kernel on the stream finishes, and holds every
   // dependent access until griddepcontrol.wait.
-  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-  if (s && cudaStreamIsCapturing(s, &cs) != cudaSuccess) cs = cudaStreamCaptureStatusActive;
-  const bool eager = cs == cudaStreamCaptureStatusNone;
   p.trigger_early = eager ? 1 : 0;
   {
     const uintptr_t w_lo = reinterpret_cast<uintptr_t>(d.b);

@@ -158,6 +158,18 @@ __device__ __forceinline__ unsigned long long ld_acquire_gpu_u64(const unsigned 
   return v;
 }
 
+// Strong (relaxed, GPU scope) 64-bit accesses.  An aligned 64-bit strong access is
+// single-copy atomic: a reader sees either the whole old or the whole new word,
+// which is what lets a value and the tag written beside it validate each other.
+__device__ __forceinline__ unsigned long long ld_relaxed_gpu_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_relaxed_gpu_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
 // Release/acquire fence at GPU scope (lighter than __threadfence's sequentially
 // consistent fence): before a signalling atomic it releases the writes that this
 // thread observed, after an observing atomic it acquires the writes it announced.

@@ -35,6 +35,7 @@ BINARY = {"add": 1, "sub": 2, "mul": 3, "div": 4}
 OPERAND_NONE, OPERAND_ROW, OPERAND_FULL = 0, 1, 2
 FP32_AUTO, FP32_3XTF32, FP32_FFMA = 0, 1, 2
 FLAG_FORCE_SIMT, FLAG_NO_SKINNY, FLAG_FORCE_SKINNY, FLAG_PAIR = 0x1, 0x2, 0x4, 0x8
+FLAG_SKINNY_COUNTER = 0x10
 ROUTES = {0: "none", 1: "tc_f16", 2: "tc_3xtf32", 3: "skinny", 4: "simt", 5: "flash_attn"}
 ATTN_FLAG_COMPOSED = 0x1
 ATTN_FLAG_ONE_QTILE, ATTN_FLAG_TWO_QTILE = 0x2, 0x4

@@ -103,6 +103,31 @@ def test_skinny_ragged_and_repeat(shape, tb):
         assert_half_parity(C.float().numpy(), ref, tol=4e-3)
 
 
+@pytest.mark.parametrize("shape,tb", [((1, 14336, 4096), False), ((4, 14336, 4096), False),
+                                      ((16, 14336, 4096), False), ((3, 1000, 320), False),
+                                      ((16, 384, 4160), True), ((9, 2048, 8192), False),
+                                      ((5, 65536, 128), False)])
+def test_skinny_handoffs_agree(shape, tb):
+    """The tagged hand-off (a group's last contributor polls the others' epoch-tagged
+    partials) and the arrival-counter hand-off sum the same partials in the same order:
+    bit-identical outputs, twice in a row (the second launch meets the first one's
+    tags and counters), and both within the bf16 bar of the oracle.  The last shape
+    has more units per CTA than k blocks per group, where only the counter applies."""
+    from torchcl._lib import FLAG_SKINNY_COUNTER
+    M, N, K = shape
+    X, W = _operands(41, M, N, K, torch.bfloat16, False, tb, scale_b=0.05)
+    bias = randn(43, (N,), torch.bfloat16, scale=0.1)
+    ref = oracle_gemm(X, W, trans_b=tb, operand=bias, kind="row", unary=("silu",))
+    outs = []
+    for flags in (0, FLAG_SKINNY_COUNTER, 0, FLAG_SKINNY_COUNTER):
+        C, route = run_gemm(X, W, trans_b=tb, operand=bias, kind="row", unary=("silu",), flags=flags)
+        assert route == "skinny"
+        outs.append(C.view(torch.int16))
+    for C in outs[1:]:
+        assert torch.equal(C, outs[0])
+    assert_half_parity(outs[0].view(torch.bfloat16).float().numpy(), ref, tol=4e-3)
+
+
 def test_skinny_matches_tile_route():
     M, N, K = 16, 1024, 2048
     X, W = _operands(31, M, N, K, torch.bfloat16, False, False)
