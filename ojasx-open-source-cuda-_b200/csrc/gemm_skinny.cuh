@@ -15,8 +15,12 @@
 // group).  A segment that covers its whole group is finished directly; otherwise
 // each contributor writes its fp32 partial into a scratch slot and bumps the
 // group's arrival counter, and the CTA that arrives last sums the partials in
-// contributor order (deterministic) and runs the fused epilogue.  No CTA ever
-// waits on another.
+// contributor order (deterministic) and runs the fused epilogue; no CTA waits on
+// another.  Eager launches in which no CTA covers more than one group's k blocks
+// use a faster hand-off instead: the group's last contributor, which reaches the
+// group at the end of its own stream, polls the others' epoch-tagged partials
+// (SkinnyParams::tagged) and waits only for lower-indexed CTAs, which wait on
+// nothing.  Both hand-offs add the same partials in the same order.
 //
 // Scratch per call: partial slots  groups * max_contributors * SK_TPU*16*128 fp32,
 // and one 64-bit arrival counter per group holding (launch epoch << 32 | count),
