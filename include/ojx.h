@@ -364,6 +364,12 @@ int ojx_graph_node_get(ojx_graph g, int32_t index, ojx_graph_node* out);
  * return with OJX_ERR_TIMEOUT recorded (read it with ojx_poll_device_error). */
 int ojx_debug_silence_producer_once(void);
 
+/* Test hook: in the next skinny launch that uses the tagged split-K hand-off, the
+ * contributing CTAs publish no partials, so every finishing CTA's bounded poll must
+ * expire; the launch returns with OJX_ERR_TIMEOUT recorded (ojx_poll_device_error)
+ * and the context stays usable. */
+int ojx_debug_silence_skinny_contributors_once(void);
+
 #ifdef __cplusplus
 }
 #endif

@@ -96,6 +96,7 @@ struct SkinnyParams {
   // last contributor reaches that group at the very end of its own stream.
   int tagged;
   unsigned long long* tagged_parts;
+  int silence_contributors;  // test hook: contributors publish nothing (the finishers' polls expire)
 };
 
 __device__ __forceinline__ long long unit_begin(int c, const SkinnyParams& p) {
@@ -407,7 +408,7 @@ __global__ void __launch_bounds__(SK_THREADS, 2)
                                      (static_cast<long long>(g) * p.maxc + jc) * SK_SLOT + q * 32 + lane;
           const unsigned long long tag = static_cast<unsigned long long>(p.epoch) << 32;
 #pragma unroll
-          for (int j = 0; j < SK_TPU; ++j)
+          for (int j = 0; j < SK_TPU && !p.silence_contributors; ++j)
 #pragma unroll
             for (int m = 0; m < SK_MN; ++m)
               if (m < p.M) st_relaxed_gpu_u64(slot + (j * SK_MN + m) * SK_BN, tag | __float_as_uint(v[j][m]));
@@ -772,6 +773,7 @@ int launch_skinny_gemm(const ojx_gemm_desc& d, cudaStream_t s, const Dests* dest
   const bool eager = cs == cudaStreamCaptureStatusNone;
   p.tagged = eager && !(d.flags & OJX_GEMM_FLAG_SKINNY_COUNTER) && (p.U + p.G - 1) / p.G <= p.KB ? 1 : 0;
   if (p.tagged) {
+    p.silence_contributors = g_silence_contributors_once.exchange(0);
     // Its own zero-initialised slot: the words there only ever carry the epochs of
     // earlier skinny launches (or 0), never this launch's.
     p.tagged_parts = static_cast<unsigned long long*>(

@@ -20,6 +20,8 @@ int cuda_status(cudaError_t e, const char* what);
 extern std::atomic<uint64_t> g_launches;   // kernels launched by this library
 extern std::atomic<uint64_t> g_wait_budget;  // SM cycles a device-side wait may spin
 extern std::atomic<int> g_silence_producer_once;
+// Next tagged skinny launch: contributors publish nothing (ojx_debug_silence_skinny_contributors_once).
+extern std::atomic<int> g_silence_contributors_once;
 void set_last_route(int route);
 
 struct DeviceProps {

@@ -24,6 +24,7 @@ static thread_local int t_last_route = OJX_ROUTE_NONE;
 std::atomic<uint64_t> g_launches{0};
 std::atomic<uint64_t> g_wait_budget{4000000000ull};  // about 2 s at B200 clocks
 std::atomic<int> g_silence_producer_once{0};
+std::atomic<int> g_silence_contributors_once{0};
 
 int set_error(int code, const char* fmt, ...) {
   char buf[1024];
@@ -948,6 +949,11 @@ int ojx_gemm_allgather(const ojx_gemm_desc* in, void* const* c_peers, int32_t n_
 
 int ojx_debug_silence_producer_once(void) {
   g_silence_producer_once.store(1);
+  return OJX_OK;
+}
+
+int ojx_debug_silence_skinny_contributors_once(void) {
+  g_silence_contributors_once.store(1);
   return OJX_OK;
 }
 

@@ -152,6 +152,7 @@ _SIGS = {
     "ojx_graph_node_count": ([_P, ctypes.c_int, ctypes.POINTER(ctypes.c_int32)], ctypes.c_int),
     "ojx_graph_node_get": ([_P, ctypes.c_int32, ctypes.POINTER(GraphNode)], ctypes.c_int),
     "ojx_debug_silence_producer_once": ([], ctypes.c_int),
+    "ojx_debug_silence_skinny_contributors_once": ([], ctypes.c_int),
 }
 
 _lib = None

@@ -92,6 +92,30 @@ def test_skinny_timeout_path():
     assert_half_parity(C.float().numpy(), oracle_gemm(X, W), tol=4e-3)
 
 
+def test_skinny_tagged_poll_times_out_and_context_survives():
+    """The finishing CTA of a tagged skinny launch waits (bounded) for the other
+    contributors' epoch-tagged partials.  With the contributors silenced, every
+    finisher's poll must expire: the launch reports OJX_ERR_TIMEOUT and the next
+    launch, with a new epoch, computes the right result."""
+    torchcl.init_opencl()
+    lib = L.lib()
+    X = randn(7, (4, 4096), torch.bfloat16)  # cfg4's shape: 3 contributors per group, tagged
+    W = randn(8, (4096, 14336), torch.bfloat16, scale=0.02)
+    L.check(lib.ojx_poll_device_error())
+    lib.ojx_set_wait_budget(2_000_000)  # about a millisecond
+    try:
+        lib.ojx_debug_silence_skinny_contributors_once()
+        with pytest.raises(L.TimeoutError_):
+            run_gemm(X, W)
+        assert L.ROUTES[lib.ojx_last_route()] == "skinny"
+        L.check(lib.ojx_poll_device_error())
+    finally:
+        lib.ojx_set_wait_budget(4_000_000_000)
+    C, _ = run_gemm(X, W)
+    assert_half_parity(C.float().numpy(), oracle_gemm(X, W), tol=4e-3)
+    L.check(lib.ojx_poll_device_error())
+
+
 def test_launch_counter_and_device_info():
     info = torchcl.get_device_info()
     assert info["max_compute_units"] >= 100 and "sm_10" in info["version"]
